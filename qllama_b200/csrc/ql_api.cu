@@ -1,0 +1,769 @@
+// ql_api.cu -- the C ABI (include/qllama_attn.h): contexts, the paged KV cache,
+// transactional validation and kernel dispatch.
+//
+// Validation mirrors the reference before any device work is queued:
+//   Attention::new head checks          src/transformer/layers.rs:254-275
+//   rope parameter checks               src/tensor/ops.rs:170-188
+//   i32 position conversion             src/transformer/layers.rs:403-422
+//   KvCache::update / get checks        src/kv_cache/cache.rs:90-144, 186-208
+// and uses the same message wording, so substring checks written against the
+// reference ("must continue", "exceeds cache capacity", "divisible", ...)
+// hold here too.  Sequence lengths advance only after the work is queued.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/qllama_attn.h"
+#include "ql_device.cuh"
+#include "ql_kernels.cuh"
+
+namespace {
+
+thread_local std::string g_error = "";
+
+int fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(e == cudaErrorMemoryAllocation ? QL_ERR_OOM : QL_ERR_CUDA, "%s: %s", what,
+              cudaGetErrorString(e));
+}
+
+#define QL_CUDA(call, what)                 \
+  do {                                      \
+    cudaError_t e_ = (call);                \
+    if (e_ != cudaSuccess) return cuda_fail(e_, what); \
+  } while (0)
+
+size_t elem_bytes(int dt) { return dt == QL_F32 ? 4 : (dt == QL_Q8_0 ? 1 : 2); }
+
+bool valid_io_dtype(int dt) { return dt == QL_F32 || dt == QL_F16 || dt == QL_BF16; }
+
+std::string dims_str(const int64_t* d, int rank) {
+  std::string s = "[";
+  for (int i = 0; i < rank; ++i) {
+    if (i) s += ", ";
+    s += std::to_string(static_cast<long long>(d[i]));
+  }
+  return s + "]";
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+}  // namespace
+
+// --------------------------------------------------------------- context --
+struct ql_ctx {
+  int device = 0;
+  int num_sms = 0;
+  cudaStream_t own = nullptr;
+  cudaStream_t stream = nullptr;
+  uint32_t* status = nullptr;  // device word raised by kernels
+  void* ws = nullptr;          // workspace (staging, split partials, scratch)
+  size_t ws_bytes = 0;
+  int32_t* counters = nullptr;  // split-merge arrival counters, kept at zero
+  size_t counters_n = 0;
+};
+
+struct ql_kv {
+  ql_ctx* ctx = nullptr;
+  ql_kv_config cfg{};
+  int pages_per_seq = 0;
+  std::vector<void*> k, v;             // per layer
+  std::vector<uint16_t*> ks, vs;       // per layer, Q8_0 scales
+  std::vector<CUtensorMap> kmap, vmap;  // per layer, split-KV kernel descriptors
+  bool have_maps = false;
+  int32_t* d_table = nullptr;          // [max_batch][pages_per_seq]
+  std::vector<int32_t> table;          // host mirror
+  std::vector<int32_t> seq_pages;      // pages owned per sequence
+  std::vector<int32_t> free_pages;     // stack of free page ids
+  std::vector<int64_t> len;            // [layer][seq] written prefix
+  double2* d_rope = nullptr;           // [max_seq_len][head_dim/2] (cos, sin)
+  float rope_theta = 0.f;
+};
+
+namespace {
+
+int ensure_ws(ql_ctx* c, size_t bytes) {
+  if (bytes <= c->ws_bytes) return QL_OK;
+  QL_CUDA(cudaStreamSynchronize(c->stream), "synchronize before growing workspace");
+  if (c->ws) cudaFree(c->ws);
+  c->ws = nullptr;
+  c->ws_bytes = 0;
+  size_t want = bytes + bytes / 4 + (1 << 20);
+  QL_CUDA(cudaMalloc(&c->ws, want), "allocate workspace");
+  c->ws_bytes = want;
+  return QL_OK;
+}
+
+int ensure_counters(ql_ctx* c, size_t n) {
+  if (n <= c->counters_n) return QL_OK;
+  QL_CUDA(cudaStreamSynchronize(c->stream), "synchronize before growing counters");
+  if (c->counters) cudaFree(c->counters);
+  c->counters = nullptr;
+  c->counters_n = 0;
+  size_t want = n + n / 2 + 1024;
+  QL_CUDA(cudaMalloc(&c->counters, want * sizeof(int32_t)), "allocate counters");
+  QL_CUDA(cudaMemset(c->counters, 0, want * sizeof(int32_t)), "zero counters");
+  c->counters_n = want;
+  return QL_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+ql::CacheView view_of(const ql_kv* kv, int layer) {
+  ql::CacheView c;
+  c.k = kv->k[layer];
+  c.v = kv->v[layer];
+  c.k_scale = kv->cfg.dtype == QL_Q8_0 ? kv->ks[layer] : nullptr;
+  c.v_scale = kv->cfg.dtype == QL_Q8_0 ? kv->vs[layer] : nullptr;
+  c.block_table = kv->d_table;
+  c.pages_per_seq = kv->pages_per_seq;
+  c.num_pages = kv->cfg.num_pages;
+  c.page = kv->cfg.page_size;
+  c.hkv = kv->cfg.num_kv_heads;
+  c.hd = kv->cfg.head_dim;
+  c.dtype = kv->cfg.dtype;
+  return c;
+}
+
+int encode_map(CUtensorMap* m, void* base, int dtype, int hd, uint64_t rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return fail(QL_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const bool q8 = dtype == QL_Q8_0;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(hd), rows};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(hd) * (q8 ? 1 : 2)};
+  cuuint32_t box[2] = {q8 ? 128u : 64u, static_cast<cuuint32_t>(ql::kTile)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, q8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, base,
+                  dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return QL_OK;
+}
+
+// Builds (once per theta) the f64 (cos, sin) table of every position with the
+// reference formula: freq_i = theta^(-2i/hd) via pow, angle = pos * freq_i
+// (src/tensor/ops.rs:193-207), evaluated by the host libm as the reference does.
+int ensure_rope(ql_kv* kv, float theta) {
+  if (kv->d_rope && kv->rope_theta == theta) return QL_OK;
+  const int hd = kv->cfg.head_dim, pairs = hd / 2, n = kv->cfg.max_seq_len;
+  std::vector<double> freq(pairs);
+  for (int p = 0; p < pairs; ++p)
+    freq[p] = std::pow(static_cast<double>(theta), -2.0 * static_cast<double>(p) / hd);
+  std::vector<double2> tab(static_cast<size_t>(n) * pairs);
+  for (int pos = 0; pos < n; ++pos)
+    for (int p = 0; p < pairs; ++p) {
+      const double ang = static_cast<double>(pos) * freq[p];
+      tab[static_cast<size_t>(pos) * pairs + p] = make_double2(std::cos(ang), std::sin(ang));
+    }
+  if (!kv->d_rope) {
+    QL_CUDA(cudaMalloc(&kv->d_rope, std::max<size_t>(1, tab.size()) * sizeof(double2)),
+            "allocate rope table");
+  }
+  QL_CUDA(cudaStreamSynchronize(kv->ctx->stream), "synchronize before rope table upload");
+  QL_CUDA(cudaMemcpy(kv->d_rope, tab.data(), tab.size() * sizeof(double2),
+                     cudaMemcpyHostToDevice),
+          "upload rope table");
+  kv->rope_theta = theta;
+  return QL_OK;
+}
+
+// Gives every listed sequence the pages its new length needs; rolls back on
+// exhaustion so that the call stays transactional.
+int reserve_pages(ql_kv* kv, const std::vector<int32_t>& seqs, const std::vector<int64_t>& ends) {
+  const int P = kv->cfg.page_size, pps = kv->pages_per_seq;
+  std::vector<std::pair<int, int>> taken;  // (seq, logical page)
+  bool changed = false;
+  for (size_t i = 0; i < seqs.size(); ++i) {
+    const int s = seqs[i];
+    const int need = static_cast<int>((ends[i] + P - 1) / P);
+    while (kv->seq_pages[s] < need) {
+      if (kv->free_pages.empty()) {
+        for (auto it = taken.rbegin(); it != taken.rend(); ++it) {
+          kv->free_pages.push_back(kv->table[static_cast<size_t>(it->first) * pps + it->second]);
+          kv->table[static_cast<size_t>(it->first) * pps + it->second] = -1;
+          kv->seq_pages[it->first]--;
+        }
+        return fail(QL_ERR_OOM, "KV page pool exhausted (%d pages of %d positions)",
+                    kv->cfg.num_pages, P);
+      }
+      const int page = kv->free_pages.back();
+      kv->free_pages.pop_back();
+      kv->table[static_cast<size_t>(s) * pps + kv->seq_pages[s]] = page;
+      taken.emplace_back(s, kv->seq_pages[s]);
+      kv->seq_pages[s]++;
+      changed = true;
+    }
+  }
+  if (changed) {
+    QL_CUDA(cudaStreamSynchronize(kv->ctx->stream), "synchronize before block-table upload");
+    QL_CUDA(cudaMemcpy(kv->d_table, kv->table.data(), kv->table.size() * sizeof(int32_t),
+                       cudaMemcpyHostToDevice),
+            "upload block table");
+  }
+  return QL_OK;
+}
+
+int64_t& len_at(ql_kv* kv, int layer, int seq) {
+  return kv->len[static_cast<size_t>(layer) * kv->cfg.max_batch + seq];
+}
+
+int check_status(ql_ctx* c) {
+  uint32_t st = 0;
+  QL_CUDA(cudaMemcpy(&st, c->status, sizeof st, cudaMemcpyDeviceToHost), "read status word");
+  if (st) {
+    cudaMemset(c->status, 0, sizeof(uint32_t));
+    return fail(QL_ERR_DEVICE, "a kernel reported status 0x%x (%s)", st,
+                (st & ql::kStatusWaitTimeout) ? "a pipeline wait timed out"
+                                              : "a block-table entry was out of range");
+  }
+  return QL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ql_version(void) { return "qllama_b200 0.1 (sm_100a)"; }
+
+const char* ql_last_error(void) { return g_error.c_str(); }
+
+int ql_ctx_create(int device, ql_ctx** out) {
+  if (!out) return fail(QL_ERR_INVALID, "ql_ctx_create: out is NULL");
+  *out = nullptr;
+  int n = 0;
+  cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess || n == 0)
+    return fail(QL_ERR_NO_DEVICE, "no CUDA device is available (%s)",
+                e == cudaSuccess ? "none found" : cudaGetErrorString(e));
+  if (device < 0 || device >= n)
+    return fail(QL_ERR_INVALID, "device %d out of range (%d devices)", device, n);
+  cudaDeviceProp prop;
+  QL_CUDA(cudaGetDeviceProperties(&prop, device), "query device");
+  if (prop.major != 10)
+    return fail(QL_ERR_UNSUPPORTED, "this build targets sm_100a (B200); device %d is sm_%d%d",
+                device, prop.major, prop.minor);
+  QL_CUDA(cudaSetDevice(device), "set device");
+  ql_ctx* c = new ql_ctx;
+  c->device = device;
+  c->num_sms = prop.multiProcessorCount;
+  e = cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&c->status, sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(uint32_t));
+  if (e != cudaSuccess) {
+    ql_ctx_destroy(c);
+    return cuda_fail(e, "create context");
+  }
+  c->stream = c->own;
+  *out = c;
+  return QL_OK;
+}
+
+int ql_ctx_destroy(ql_ctx* c) {
+  if (!c) return QL_OK;
+  cudaSetDevice(c->device);
+  if (c->own) cudaStreamSynchronize(c->own);
+  if (c->ws) cudaFree(c->ws);
+  if (c->counters) cudaFree(c->counters);
+  if (c->status) cudaFree(c->status);
+  if (c->own) cudaStreamDestroy(c->own);
+  delete c;
+  return QL_OK;
+}
+
+int ql_ctx_set_stream(ql_ctx* c, void* stream) {
+  if (!c) return fail(QL_ERR_INVALID, "ql_ctx_set_stream: ctx is NULL");
+  c->stream = stream ? static_cast<cudaStream_t>(stream) : c->own;
+  return QL_OK;
+}
+
+int ql_ctx_synchronize(ql_ctx* c) {
+  if (!c) return fail(QL_ERR_INVALID, "ql_ctx_synchronize: ctx is NULL");
+  QL_CUDA(cudaSetDevice(c->device), "set device");
+  QL_CUDA(cudaStreamSynchronize(c->stream), "synchronize");
+  return check_status(c);
+}
+
+int ql_kv_create(ql_ctx* c, const ql_kv_config* cfg_in, ql_kv** out) {
+  if (!c || !cfg_in || !out) return fail(QL_ERR_INVALID, "ql_kv_create: NULL argument");
+  *out = nullptr;
+  ql_kv_config cfg = *cfg_in;
+  if (cfg.page_size == 0) cfg.page_size = ql::kTile;
+  if (cfg.max_batch == 0) cfg.max_batch = 1;
+  if (cfg.num_layers < 0 || cfg.max_seq_len < 0 || cfg.num_kv_heads <= 0 || cfg.head_dim <= 0 ||
+      cfg.max_batch < 0 || cfg.num_pages < 0)
+    return fail(QL_ERR_INVALID,
+                "KV cache needs num_layers >= 0, max_seq_len >= 0, num_kv_heads > 0, head_dim > 0");
+  if (cfg.dtype < QL_F32 || cfg.dtype > QL_Q8_0)
+    return fail(QL_ERR_INVALID, "unknown KV cache dtype %d", cfg.dtype);
+  if (cfg.page_size % ql::kTile != 0)
+    return fail(QL_ERR_INVALID, "page_size %d must be a positive multiple of %d", cfg.page_size,
+                ql::kTile);
+  if (cfg.dtype == QL_Q8_0 && cfg.head_dim % 32 != 0)
+    return fail(QL_ERR_INVALID, "Q8_0 storage needs head_dim divisible by 32, got %d",
+                cfg.head_dim);
+  QL_CUDA(cudaSetDevice(c->device), "set device");
+  ql_kv* kv = new ql_kv;
+  kv->ctx = c;
+  kv->pages_per_seq = (cfg.max_seq_len + cfg.page_size - 1) / cfg.page_size;
+  if (cfg.num_pages == 0) cfg.num_pages = cfg.max_batch * std::max(1, kv->pages_per_seq);
+  kv->cfg = cfg;
+  const size_t rows = static_cast<size_t>(cfg.num_pages) * cfg.num_kv_heads * cfg.page_size;
+  const size_t bytes = rows * cfg.head_dim * elem_bytes(cfg.dtype);
+  auto cleanup = [&](int code) {
+    ql_kv_destroy(kv);
+    return code;
+  };
+  for (int l = 0; l < cfg.num_layers; ++l) {
+    void *kp = nullptr, *vp = nullptr;
+    cudaError_t e = cudaMalloc(&kp, std::max<size_t>(bytes, 256));
+    if (e == cudaSuccess) e = cudaMalloc(&vp, std::max<size_t>(bytes, 256));
+    if (e == cudaSuccess) e = cudaMemset(kp, 0, std::max<size_t>(bytes, 256));
+    if (e == cudaSuccess) e = cudaMemset(vp, 0, std::max<size_t>(bytes, 256));
+    kv->k.push_back(kp);
+    kv->v.push_back(vp);
+    if (e != cudaSuccess) return cleanup(cuda_fail(e, "allocate KV pool"));
+    if (cfg.dtype == QL_Q8_0) {
+      const size_t sb = std::max<size_t>(rows * (cfg.head_dim / 32) * 2, 256);
+      uint16_t *a = nullptr, *b = nullptr;
+      e = cudaMalloc(&a, sb);
+      if (e == cudaSuccess) e = cudaMalloc(&b, sb);
+      if (e == cudaSuccess) e = cudaMemset(a, 0, sb);
+      if (e == cudaSuccess) e = cudaMemset(b, 0, sb);
+      kv->ks.push_back(a);
+      kv->vs.push_back(b);
+      if (e != cudaSuccess) return cleanup(cuda_fail(e, "allocate Q8_0 scales"));
+    }
+  }
+  kv->table.assign(static_cast<size_t>(cfg.max_batch) * std::max(1, kv->pages_per_seq), -1);
+  kv->seq_pages.assign(cfg.max_batch, 0);
+  for (int p = cfg.num_pages - 1; p >= 0; --p) kv->free_pages.push_back(p);
+  kv->len.assign(static_cast<size_t>(std::max(1, cfg.num_layers)) * cfg.max_batch, 0);
+  cudaError_t e = cudaMalloc(&kv->d_table, kv->table.size() * sizeof(int32_t));
+  if (e == cudaSuccess)
+    e = cudaMemcpy(kv->d_table, kv->table.data(), kv->table.size() * sizeof(int32_t),
+                   cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cleanup(cuda_fail(e, "allocate block table"));
+  if (ql::splitkv_supported(cfg.head_dim, cfg.dtype, 1, cfg.page_size) && rows > 0) {
+    kv->kmap.resize(cfg.num_layers);
+    kv->vmap.resize(cfg.num_layers);
+    for (int l = 0; l < cfg.num_layers; ++l) {
+      int r = encode_map(&kv->kmap[l], kv->k[l], cfg.dtype, cfg.head_dim, rows);
+      if (r == QL_OK) r = encode_map(&kv->vmap[l], kv->v[l], cfg.dtype, cfg.head_dim, rows);
+      if (r != QL_OK) return cleanup(r);
+    }
+    kv->have_maps = true;
+  }
+  *out = kv;
+  return QL_OK;
+}
+
+int ql_kv_destroy(ql_kv* kv) {
+  if (!kv) return QL_OK;
+  cudaSetDevice(kv->ctx->device);
+  cudaStreamSynchronize(kv->ctx->stream);
+  for (void* p : kv->k) cudaFree(p);
+  for (void* p : kv->v) cudaFree(p);
+  for (void* p : kv->ks) cudaFree(p);
+  for (void* p : kv->vs) cudaFree(p);
+  if (kv->d_table) cudaFree(kv->d_table);
+  if (kv->d_rope) cudaFree(kv->d_rope);
+  delete kv;
+  return QL_OK;
+}
+
+int ql_kv_clear(ql_kv* kv) {
+  if (!kv) return fail(QL_ERR_INVALID, "ql_kv_clear: kv is NULL");
+  // Lengths back to zero; buffers (and pages) stay, as in cache.rs:231-239.
+  std::fill(kv->len.begin(), kv->len.end(), 0);
+  return QL_OK;
+}
+
+int ql_kv_clear_seq(ql_kv* kv, int32_t seq) {
+  if (!kv) return fail(QL_ERR_INVALID, "ql_kv_clear_seq: kv is NULL");
+  if (seq < 0 || seq >= kv->cfg.max_batch)
+    return fail(QL_ERR_INVALID, "sequence %d out of range (cache has %d slots)", seq,
+                kv->cfg.max_batch);
+  // Stale rows stay in the pages; lengths make them unreachable (cache.rs:231-234).
+  for (int l = 0; l < kv->cfg.num_layers; ++l) len_at(kv, l, seq) = 0;
+  const int pps = kv->pages_per_seq;
+  if (kv->seq_pages[seq] > 0) {
+    QL_CUDA(cudaSetDevice(kv->ctx->device), "set device");
+    QL_CUDA(cudaStreamSynchronize(kv->ctx->stream), "synchronize before releasing pages");
+    for (int i = kv->seq_pages[seq] - 1; i >= 0; --i) {
+      kv->free_pages.push_back(kv->table[static_cast<size_t>(seq) * pps + i]);
+      kv->table[static_cast<size_t>(seq) * pps + i] = -1;
+    }
+    kv->seq_pages[seq] = 0;
+  }
+  return QL_OK;
+}
+
+int ql_kv_seq_len(const ql_kv* kv, int32_t seq, int64_t* out_len) {
+  if (!kv || !out_len) return fail(QL_ERR_INVALID, "ql_kv_seq_len: NULL argument");
+  if (seq < 0 || seq >= kv->cfg.max_batch)
+    return fail(QL_ERR_INVALID, "sequence %d out of range (cache has %d slots)", seq,
+                kv->cfg.max_batch);
+  *out_len = kv->cfg.num_layers ? kv->len[seq] : 0;
+  return QL_OK;
+}
+
+int ql_kv_layer_len(const ql_kv* kv, int32_t layer, int32_t seq, int64_t* out_len) {
+  if (!kv || !out_len) return fail(QL_ERR_INVALID, "ql_kv_layer_len: NULL argument");
+  if (layer < 0 || layer >= kv->cfg.num_layers)
+    return fail(QL_ERR_INVALID, "KV cache layer index %d out of range (cache has %d layers)",
+                layer, kv->cfg.num_layers);
+  if (seq < 0 || seq >= kv->cfg.max_batch)
+    return fail(QL_ERR_INVALID, "sequence %d out of range (cache has %d slots)", seq,
+                kv->cfg.max_batch);
+  *out_len = kv->len[static_cast<size_t>(layer) * kv->cfg.max_batch + seq];
+  return QL_OK;
+}
+
+int ql_kv_update(ql_ctx* c, ql_kv* kv, int32_t layer, int32_t seq, const void* k,
+                 const int64_t* k_dims, int32_t k_rank, const void* v, const int64_t* v_dims,
+                 int32_t v_rank, int32_t in_dtype, const int32_t* positions, int64_t n_positions,
+                 int32_t mem) {
+  if (!c || !kv || (!k_dims && k_rank) || (!v_dims && v_rank))
+    return fail(QL_ERR_INVALID, "ql_kv_update: NULL argument");
+  const int hkv = kv->cfg.num_kv_heads, hd = kv->cfg.head_dim;
+  if (layer < 0 || layer >= kv->cfg.num_layers)
+    return fail(QL_ERR_INVALID, "KV cache layer index %d out of range (cache has %d layers)",
+                layer, kv->cfg.num_layers);
+  if (seq < 0 || seq >= kv->cfg.max_batch)
+    return fail(QL_ERR_INVALID, "sequence %d out of range (cache has %d slots)", seq,
+                kv->cfg.max_batch);
+  const std::string kd = dims_str(k_dims, k_rank), vd = dims_str(v_dims, v_rank);
+  if (k_rank != 3 || k_dims[1] != hkv || k_dims[2] != hd)
+    return fail(QL_ERR_INVALID, "K shape %s does not match cache [_, %d, %d]", kd.c_str(), hkv,
+                hd);
+  bool same = v_rank == k_rank;
+  for (int i = 0; same && i < k_rank; ++i) same = v_dims[i] == k_dims[i];
+  if (!same) return fail(QL_ERR_INVALID, "K/V shape mismatch: K %s, V %s", kd.c_str(), vd.c_str());
+  const int64_t n = k_dims[0];
+  if (n_positions != n)
+    return fail(QL_ERR_INVALID, "K batch is %lld token(s) but got %lld position(s)",
+                (long long)n, (long long)n_positions);
+  if (!valid_io_dtype(in_dtype)) return fail(QL_ERR_INVALID, "unknown input dtype %d", in_dtype);
+  if (n > 0 && (!positions || !k || !v)) return fail(QL_ERR_INVALID, "ql_kv_update: NULL data");
+  const int64_t cur = len_at(kv, layer, seq);
+  for (int64_t i = 0; i < n; ++i) {
+    const int32_t p = positions[i];
+    if (p < 0) return fail(QL_ERR_INVALID, "positions[%lld] = %d is negative", (long long)i, p);
+    if (p != cur + i)
+      return fail(QL_ERR_INVALID,
+                  "positions[%lld] = %d must continue from current_len (expected %lld); "
+                  "skipping, backward, or double writes are not allowed",
+                  (long long)i, p, (long long)(cur + i));
+    if (p >= kv->cfg.max_seq_len)
+      return fail(QL_ERR_INVALID, "positions[%lld] = %d exceeds cache capacity %d", (long long)i,
+                  p, kv->cfg.max_seq_len);
+  }
+  if (n == 0) return QL_OK;  // empty batch: no-op (cache.rs:77-78)
+  if (n > INT32_MAX / (hkv * 32)) return fail(QL_ERR_INVALID, "batch too large");
+  QL_CUDA(cudaSetDevice(c->device), "set device");
+  int r = reserve_pages(kv, {seq}, {cur + n});
+  if (r != QL_OK) return r;
+  const size_t in_bytes = static_cast<size_t>(n) * hkv * hd * elem_bytes(in_dtype);
+  const void *kd_ptr = k, *vd_ptr = v;
+  if (mem == QL_MEM_HOST) {
+    r = ensure_ws(c, 2 * align256(in_bytes));
+    if (r != QL_OK) return r;
+    char* w = static_cast<char*>(c->ws);
+    QL_CUDA(cudaMemcpyAsync(w, k, in_bytes, cudaMemcpyHostToDevice, c->stream), "copy K");
+    QL_CUDA(cudaMemcpyAsync(w + align256(in_bytes), v, in_bytes, cudaMemcpyHostToDevice,
+                            c->stream),
+            "copy V");
+    kd_ptr = w;
+    vd_ptr = w + align256(in_bytes);
+  }
+  ql::AppendArgs a{};
+  a.k = kd_ptr;
+  a.v = vd_ptr;
+  a.in_dtype = in_dtype;
+  a.batch = 1;
+  a.new_len = static_cast<int32_t>(n);
+  a.rope = nullptr;  // update() stores K as given (already rotated)
+  a.cache = view_of(kv, layer);
+  a.status = c->status;
+  a.seqs.seq[0] = seq;
+  a.seqs.start[0] = static_cast<int32_t>(cur);
+  QL_CUDA(ql::launch_append(a, c->stream), "launch append");
+  if (mem == QL_MEM_HOST) QL_CUDA(cudaStreamSynchronize(c->stream), "synchronize update");
+  len_at(kv, layer, seq) = cur + n;
+  return QL_OK;
+}
+
+int ql_kv_get(ql_ctx* c, const ql_kv* kv, int32_t layer, int32_t seq, const int32_t* positions,
+              int64_t n_positions, float* k_out, float* v_out, int32_t mem) {
+  if (!c || !kv) return fail(QL_ERR_INVALID, "ql_kv_get: NULL argument");
+  if (layer < 0 || layer >= kv->cfg.num_layers)
+    return fail(QL_ERR_INVALID, "KV cache layer index %d out of range (cache has %d layers)",
+                layer, kv->cfg.num_layers);
+  if (seq < 0 || seq >= kv->cfg.max_batch)
+    return fail(QL_ERR_INVALID, "sequence %d out of range (cache has %d slots)", seq,
+                kv->cfg.max_batch);
+  const int64_t cur = kv->len[static_cast<size_t>(layer) * kv->cfg.max_batch + seq];
+  for (int64_t i = 0; i < n_positions; ++i) {
+    const int32_t p = positions[i];
+    if (p < 0) return fail(QL_ERR_INVALID, "positions[%lld] = %d is negative", (long long)i, p);
+    if (p >= cur)
+      return fail(QL_ERR_INVALID,
+                  "positions[%lld] = %d is at or beyond the written prefix (current_len %lld)",
+                  (long long)i, p, (long long)cur);
+  }
+  if (n_positions == 0) return QL_OK;
+  if (!k_out || !v_out) return fail(QL_ERR_INVALID, "ql_kv_get: NULL output");
+  QL_CUDA(cudaSetDevice(c->device), "set device");
+  const size_t ob = static_cast<size_t>(n_positions) * kv->cfg.num_kv_heads * kv->cfg.head_dim *
+                    sizeof(float);
+  const size_t pb = static_cast<size_t>(n_positions) * sizeof(int32_t);
+  int r = ensure_ws(c, align256(pb) + (mem == QL_MEM_HOST ? 2 * align256(ob) : 0));
+  if (r != QL_OK) return r;
+  char* w = static_cast<char*>(c->ws);
+  QL_CUDA(cudaMemcpyAsync(w, positions, pb, cudaMemcpyHostToDevice, c->stream), "copy positions");
+  ql::GatherArgs g{};
+  g.positions = reinterpret_cast<const int32_t*>(w);
+  g.n = static_cast<int32_t>(n_positions);
+  g.seq = seq;
+  g.k_out = mem == QL_MEM_HOST ? reinterpret_cast<float*>(w + align256(pb)) : k_out;
+  g.v_out = mem == QL_MEM_HOST ? reinterpret_cast<float*>(w + align256(pb) + align256(ob)) : v_out;
+  g.cache = view_of(kv, layer);
+  QL_CUDA(ql::launch_gather(g, c->stream), "launch gather");
+  if (mem == QL_MEM_HOST) {
+    QL_CUDA(cudaMemcpyAsync(k_out, g.k_out, ob, cudaMemcpyDeviceToHost, c->stream), "copy K out");
+    QL_CUDA(cudaMemcpyAsync(v_out, g.v_out, ob, cudaMemcpyDeviceToHost, c->stream), "copy V out");
+  }
+  QL_CUDA(cudaStreamSynchronize(c->stream), "synchronize get");
+  return QL_OK;
+}
+
+int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
+  if (!c || !kv || !a) return fail(QL_ERR_INVALID, "ql_attn_forward: NULL argument");
+  const int hq = a->num_heads, hkv = a->num_kv_heads, hd = a->head_dim;
+  // Attention::new (layers.rs:254-261)
+  if (hq <= 0 || hkv <= 0 || hd <= 0)
+    return fail(QL_ERR_INVALID, "Attention head counts and head_dim must be positive");
+  if (hq % hkv != 0)
+    return fail(QL_ERR_INVALID, "num_heads %d must be divisible by num_kv_heads %d", hq, hkv);
+  if (a->batch < 1 || a->new_len < 0)
+    return fail(QL_ERR_INVALID, "batch must be >= 1 and new_len >= 0 (got %d, %d)", a->batch,
+                a->new_len);
+  if (a->batch > ql::kMaxBatch || a->batch > kv->cfg.max_batch)
+    return fail(QL_ERR_INVALID, "batch %d exceeds the limit (%d per call, %d cache slots)",
+                a->batch, ql::kMaxBatch, kv->cfg.max_batch);
+  if (!a->seq_ids || !a->start_pos) return fail(QL_ERR_INVALID, "seq_ids/start_pos are NULL");
+  // rope parameters (ops.rs:170-182)
+  if ((hd & 1) != 0)
+    return fail(QL_ERR_INVALID,
+                "RoPE requires shape [seq_len, ..., head_dim] with a positive even head_dim");
+  if (!std::isfinite(a->rope_theta) || a->rope_theta <= 0.f)
+    return fail(QL_ERR_INVALID, "RoPE theta must be finite and positive");
+  if (!valid_io_dtype(a->in_dtype) || !valid_io_dtype(a->out_dtype))
+    return fail(QL_ERR_INVALID, "unknown input/output dtype (%d, %d)", a->in_dtype, a->out_dtype);
+  if (a->mem != QL_MEM_DEVICE && a->mem != QL_MEM_HOST)
+    return fail(QL_ERR_INVALID, "unknown memory kind %d", a->mem);
+  const int layer = a->layer_idx;
+  if (layer < 0 || layer >= kv->cfg.num_layers)
+    return fail(QL_ERR_INVALID, "KV cache layer index %d out of range (cache has %d layers)",
+                layer, kv->cfg.num_layers);
+  const int n = a->new_len;
+  if (hkv != kv->cfg.num_kv_heads || hd != kv->cfg.head_dim)
+    return fail(QL_ERR_INVALID, "K shape [%d, %d, %d] does not match cache [_, %d, %d]", n, hkv,
+                hd, kv->cfg.num_kv_heads, kv->cfg.head_dim);
+  std::vector<int32_t> seqs(a->batch);
+  std::vector<int64_t> ends(a->batch);
+  std::vector<char> seen(kv->cfg.max_batch, 0);
+  for (int b = 0; b < a->batch; ++b) {
+    const int s = a->seq_ids[b];
+    if (s < 0 || s >= kv->cfg.max_batch)
+      return fail(QL_ERR_INVALID, "sequence %d out of range (cache has %d slots)", s,
+                  kv->cfg.max_batch);
+    if (seen[s]) return fail(QL_ERR_INVALID, "sequence %d appears twice in one call", s);
+    seen[s] = 1;
+    const int64_t start = a->start_pos[b];
+    if (start < 0) return fail(QL_ERR_INVALID, "start_pos %lld is negative", (long long)start);
+    const int64_t last = start + (n > 0 ? n - 1 : 0);
+    if (last > INT32_MAX)
+      return fail(QL_ERR_INVALID, "position %lld exceeds the i32 range the cache uses",
+                  (long long)last);
+    const int64_t cur = len_at(kv, layer, s);
+    if (n > 0) {
+      if (start != cur)
+        return fail(QL_ERR_INVALID,
+                    "positions[0] = %lld must continue from current_len (expected %lld); "
+                    "skipping, backward, or double writes are not allowed",
+                    (long long)start, (long long)cur);
+      if (start + n > kv->cfg.max_seq_len)
+        return fail(QL_ERR_INVALID, "positions[%lld] = %lld exceeds cache capacity %d",
+                    (long long)(kv->cfg.max_seq_len - start),
+                    (long long)kv->cfg.max_seq_len, kv->cfg.max_seq_len);
+    } else if (start > cur) {
+      return fail(QL_ERR_INVALID,
+                  "positions[%lld] = %lld is at or beyond the written prefix (current_len %lld)",
+                  (long long)cur, (long long)cur, (long long)cur);
+    }
+    seqs[b] = s;
+    ends[b] = start + n;
+  }
+  if (n == 0) return QL_OK;  // empty batch (transformer_forward.rs:919-946)
+  if (!a->q || !a->k || !a->v || !a->out) return fail(QL_ERR_INVALID, "q/k/v/out is NULL");
+  QL_CUDA(cudaSetDevice(c->device), "set device");
+  int r = reserve_pages(kv, seqs, ends);
+  if (r != QL_OK) return r;
+  r = ensure_rope(kv, a->rope_theta);
+  if (r != QL_OK) return r;
+
+  const int group = hq / hkv;
+  const int jobs = a->batch * n;
+  const size_t qn = static_cast<size_t>(jobs) * hq * hd, kn = static_cast<size_t>(jobs) * hkv * hd;
+  const size_t ib = elem_bytes(a->in_dtype), obb = elem_bytes(a->out_dtype);
+  const bool fast = kv->have_maps && ql::splitkv_supported(hd, kv->cfg.dtype, group,
+                                                          kv->cfg.page_size);
+  // split planning for the tensor-core kernel
+  int max_tiles = 0;
+  long long total_tiles = 0;
+  int max_len = 0;
+  for (int b = 0; b < a->batch; ++b) {
+    const int64_t end = ends[b];
+    max_len = std::max<int>(max_len, static_cast<int>(end));
+    const int tl = static_cast<int>((end + ql::kTile - 1) / ql::kTile);
+    max_tiles = std::max(max_tiles, tl);
+    total_tiles += static_cast<long long>(tl) * n * hkv;  // upper bound over the batch's tokens
+  }
+  int tps = max_tiles, max_splits = 1;
+  if (fast) {
+    const long long slots = 2LL * c->num_sms;
+    if (static_cast<long long>(jobs) * hkv < 2 * slots) {
+      tps = static_cast<int>(std::max<long long>(1, (total_tiles + 4 * slots - 1) / (4 * slots)));
+      tps = std::max(tps, (max_tiles + 63) / 64);
+    }
+    max_splits = (max_tiles + tps - 1) / tps;
+  }
+  // workspace: [staged q][k][v][out][part_o][part_ml][generic scratch f32][f64]
+  size_t off = 0;
+  const size_t o_q = off; off += align256(a->mem == QL_MEM_HOST ? qn * ib : 0);
+  const size_t o_k = off; off += align256(a->mem == QL_MEM_HOST ? kn * ib : 0);
+  const size_t o_v = off; off += align256(a->mem == QL_MEM_HOST ? kn * ib : 0);
+  const size_t o_o = off; off += align256(a->mem == QL_MEM_HOST ? qn * obb : 0);
+  const size_t o_po = off;
+  if (fast && max_splits > 1)
+    off += align256(static_cast<size_t>(jobs) * hkv * max_splits * 8 * hd * sizeof(float));
+  const size_t o_pm = off;
+  if (fast && max_splits > 1)
+    off += align256(static_cast<size_t>(jobs) * hkv * max_splits * 8 * 2 * sizeof(float));
+  const int gjobs = std::min(jobs, 65535);
+  const size_t o_gs = off;
+  if (!fast) off += align256(static_cast<size_t>(gjobs) * hq * max_len * sizeof(float));
+  const size_t o_gd = off;
+  if (!fast) off += align256(static_cast<size_t>(gjobs) * hq * max_len * sizeof(double));
+  r = ensure_ws(c, off);
+  if (r != QL_OK) return r;
+  if (fast && max_splits > 1) {
+    r = ensure_counters(c, static_cast<size_t>(jobs) * hkv);
+    if (r != QL_OK) return r;
+  }
+  char* w = static_cast<char*>(c->ws);
+  const void *q = a->q, *k = a->k, *v = a->v;
+  void* out = a->out;
+  if (a->mem == QL_MEM_HOST) {
+    QL_CUDA(cudaMemcpyAsync(w + o_q, a->q, qn * ib, cudaMemcpyHostToDevice, c->stream), "copy q");
+    QL_CUDA(cudaMemcpyAsync(w + o_k, a->k, kn * ib, cudaMemcpyHostToDevice, c->stream), "copy k");
+    QL_CUDA(cudaMemcpyAsync(w + o_v, a->v, kn * ib, cudaMemcpyHostToDevice, c->stream), "copy v");
+    q = w + o_q;
+    k = w + o_k;
+    v = w + o_v;
+    out = w + o_o;
+  }
+  ql::CacheView cv = view_of(kv, layer);
+  ql::SeqTable st{};
+  for (int b = 0; b < a->batch; ++b) {
+    st.seq[b] = seqs[b];
+    st.start[b] = static_cast<int32_t>(a->start_pos[b]);
+  }
+  const bool fuse = fast && n == 1;
+  if (!fuse) {
+    ql::AppendArgs ap{};
+    ap.k = k;
+    ap.v = v;
+    ap.in_dtype = a->in_dtype;
+    ap.batch = a->batch;
+    ap.new_len = n;
+    ap.rope = kv->d_rope;
+    ap.cache = cv;
+    ap.status = c->status;
+    ap.seqs = st;
+    QL_CUDA(ql::launch_append(ap, c->stream), "launch append");
+  }
+  ql::AttnArgs at{};
+  at.q = q;
+  at.k = k;
+  at.v = v;
+  at.in_dtype = a->in_dtype;
+  at.out = out;
+  at.out_dtype = a->out_dtype;
+  at.rope = kv->d_rope;
+  at.cache = cv;
+  at.hq = hq;
+  at.group = group;
+  at.batch = a->batch;
+  at.new_len = n;
+  at.scale = 1.0f / std::sqrt(static_cast<float>(hd));  // layers.rs:432
+  at.fuse_append = fuse ? 1 : 0;
+  at.tiles_per_split = tps;
+  at.max_splits = max_splits;
+  at.part_o = reinterpret_cast<float*>(w + o_po);
+  at.part_ml = reinterpret_cast<float*>(w + o_pm);
+  at.counters = c->counters;
+  at.scratch = reinterpret_cast<float*>(w + o_gs);
+  at.scratch_d = reinterpret_cast<double*>(w + o_gd);
+  at.max_len = max_len;
+  at.status = c->status;
+  at.seqs = st;
+  if (fast)
+    QL_CUDA(ql::launch_splitkv(at, &kv->kmap[layer], &kv->vmap[layer], jobs, c->stream),
+            "launch split-KV attention");
+  else
+    QL_CUDA(ql::launch_generic(at, c->stream), "launch attention");
+  if (a->mem == QL_MEM_HOST) {
+    QL_CUDA(cudaMemcpyAsync(a->out, out, qn * obb, cudaMemcpyDeviceToHost, c->stream),
+            "copy out");
+    QL_CUDA(cudaStreamSynchronize(c->stream), "synchronize forward");
+  }
+  for (int b = 0; b < a->batch; ++b) len_at(kv, layer, seqs[b]) = ends[b];
+  return QL_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,237 @@
+// ql_device.cuh -- device helpers shared by the attention kernels (sm_100a).
+//
+// Inline-PTX wrappers for mbarriers, TMA (tensor and plain bulk copies, never
+// with cluster multicast), ldmatrix and the m16n8k16 tensor-core MMA, plus
+// element conversions and the f64 RoPE rotation that reproduces the
+// reference bit for bit (src/tensor/ops.rs:207-215).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ql {
+
+enum : int { kF32 = 0, kF16 = 1, kBF16 = 2, kQ8_0 = 3 };
+
+// Bits of the context status word that kernels raise instead of trapping.
+enum : uint32_t {
+  kStatusWaitTimeout = 1u,  // an mbarrier wait ran out of iterations
+  kStatusBadPage = 2u,      // a block-table entry pointed outside the pool
+};
+
+// Time bound for every spin on an mbarrier, in nanoseconds of %globaltimer:
+// far above any legitimate wait (a TMA tile lands in microseconds), short
+// enough that a copy that never completes ends the kernel in about a second.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------- mbarrier --
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: returns false (and raises the status bit) if the phase has not
+// flipped within kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) break;
+  }
+  if (status) atomicOr(status, kStatusWaitTimeout);
+  return false;
+}
+
+// ------------------------------------------------------------------- TMA --
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled load of one box into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x,
+                                            int32_t y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Plain (untiled) bulk copy global -> shared; both addresses 16-byte aligned,
+// size a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// ------------------------------------------------------- ldmatrix / mma --
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                            uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1,
+                                                  uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+// D(16x8,f32) += A(16x16, row) * B(16x8, col); A/B f16 (BF = false) or bf16.
+template <bool BF>
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  if constexpr (BF) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+// -------------------------------------------------------------- elements --
+template <bool BF>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (BF) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+template <bool BF>
+__device__ __forceinline__ float round16(float x) {
+  if constexpr (BF) return __bfloat162float(__float2bfloat16_rn(x));
+  else return __half2float(__float2half_rn(x));
+}
+
+// Splits x into hi + lo, both representable in the 16-bit type, so that two
+// MMAs recover about twice the significand of one.
+template <bool BF>
+__device__ __forceinline__ void split16(float x, float& hi, float& lo) {
+  hi = round16<BF>(x);
+  lo = x - hi;
+}
+
+__device__ __forceinline__ float load_elem(const void* base, size_t i, int dt) {
+  if (dt == kF32) return static_cast<const float*>(base)[i];
+  if (dt == kF16) return __half2float(static_cast<const __half*>(base)[i]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]);
+}
+
+__device__ __forceinline__ void store_elem(void* base, size_t i, int dt, float x) {
+  if (dt == kF32) static_cast<float*>(base)[i] = x;
+  else if (dt == kF16) static_cast<__half*>(base)[i] = __float2half_rn(x);
+  else static_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(x);
+}
+
+// int8x4 in one word -> two f16x2 holding (b0,b1) and (b2,b3), exactly.
+// Each byte is biased to an unsigned value u = x + 128 placed in the low
+// mantissa bits of an f16 with exponent 10 (value 1024 + u); subtracting
+// 1152 leaves x.
+__device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, uint32_t& h01, uint32_t& h23) {
+  uint32_t u = w ^ 0x80808080u;
+  uint32_t lo, hi;
+  asm("prmt.b32 %0, %1, %2, 0x7170;" : "=r"(lo) : "r"(u), "r"(0x64646464u));
+  asm("prmt.b32 %0, %1, %2, 0x7372;" : "=r"(hi) : "r"(u), "r"(0x64646464u));
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));
+  __half2 a = __hsub2(*reinterpret_cast<__half2*>(&lo), bias);
+  __half2 b = __hsub2(*reinterpret_cast<__half2*>(&hi), bias);
+  h01 = *reinterpret_cast<uint32_t*>(&a);
+  h23 = *reinterpret_cast<uint32_t*>(&b);
+}
+
+// ------------------------------------------------------------------ RoPE --
+// The reference rotates each adjacent pair in f64 and casts to f32:
+//   y0 = (x0*cos - x1*sin) as f32, y1 = (x0*sin + x1*cos) as f32
+// (src/tensor/ops.rs:212-215).  The explicit _rn intrinsics keep the
+// compiler from contracting the products into FMAs, so the result equals
+// the reference's bit for bit given the same f64 cos/sin (taken from a table
+// the host builds with the reference's formula).
+__device__ __forceinline__ void rope_pair(float x0, float x1, double2 cs, float& y0,
+                                          float& y1) {
+  double a = __dmul_rn(static_cast<double>(x0), cs.x);
+  double b = __dmul_rn(static_cast<double>(x1), cs.y);
+  double c = __dmul_rn(static_cast<double>(x0), cs.y);
+  double d = __dmul_rn(static_cast<double>(x1), cs.x);
+  y0 = __double2float_rn(__dsub_rn(a, b));
+  y1 = __double2float_rn(__dadd_rn(c, d));
+}
+
+// Q8_0 quantisation of one 32-value block held as 16 pairs by 16 consecutive
+// lanes (lane & 15 = pair index within the block).  Same rule as the GGUF
+// reference quantiser: d = amax/127, id = 1/d (0 if d == 0), q = round(x*id)
+// with ties away from zero, scale stored as f16(d).
+__device__ __forceinline__ void q8_0_pair(float x0, float x1, int8_t& q0, int8_t& q1,
+                                          __half& scale) {
+  float amax = fmaxf(fabsf(x0), fabsf(x1));
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  float d = amax / 127.0f;
+  float id = d != 0.0f ? 1.0f / d : 0.0f;
+  float r0 = roundf(x0 * id), r1 = roundf(x1 * id);
+  q0 = static_cast<int8_t>(r0 == r0 ? static_cast<int>(r0) : 0);
+  q1 = static_cast<int8_t>(r1 == r1 ? static_cast<int>(r1) : 0);
+  scale = __float2half_rn(d);
+}
+
+}  // namespace ql

@@ -1,0 +1,698 @@
+// ql_kernels.cu -- the attention hot path kernels for B200 (sm_100a).
+//
+//  append_kernel    RoPE on new K rows + conversion/quantisation of K and V into
+//                   the paged cache (reference: ops.rs:168-220 rope,
+//                   cache.rs:146-163 update writes).
+//  splitkv_kernel   causal GQA attention of one query token per CTA job over
+//                   the cached prefix, split along the KV length.  K/V tiles
+//                   are streamed by TMA into swizzled shared memory behind an
+//                   mbarrier pipeline (one producer warp, four consumer warps);
+//                   QK^T and PV run on the tensor cores with f32 accumulation;
+//                   online softmax in registers; the last CTA of a job merges
+//                   the splits.  For single-token decode the same CTA also
+//                   rotates and appends the new K/V (fused prologue).
+//                   (reference: layers.rs:425-455 with cache.rs:185-229 get)
+//  generic_kernel   CUDA-core path for f32 caches and other head sizes; it keeps
+//                   the reference's operation order (sequential f32 dot
+//                   products without FMA, f64 softmax with a sequential sum,
+//                   sequential f32 P.V) so its results track the reference to
+//                   the last bit in all but rare f64-exp rounding cases.
+//  gather_kernel    KvCache::get (cache.rs:185-229) into f32.
+#include <math_constants.h>
+
+#include "ql_device.cuh"
+#include "ql_kernels.cuh"
+
+namespace ql {
+
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ int64_t cache_row(const CacheView& c, int seq, int pos, int h,
+                                             uint32_t* status, bool& ok) {
+  int page = c.block_table[static_cast<size_t>(seq) * c.pages_per_seq + pos / c.page];
+  if (page < 0 || page >= c.num_pages) {
+    ok = false;
+    if (status) atomicOr(status, kStatusBadPage);
+    return 0;
+  }
+  ok = true;
+  return (static_cast<int64_t>(page) * c.hkv + h) * c.page + pos % c.page;
+}
+
+// One warp writes one cache row (one position of one KV head): K rotated
+// when rope_row is given, V as is, both converted to the cache type.
+__device__ void append_row(const void* kin, const void* vin, int in_dt, size_t in_off,
+                           const double2* rope_row, const CacheView& c, int64_t dst, int lane) {
+  const int hd = c.hd;
+  const int pairs = hd / 2;
+  for (int base = 0; base < pairs; base += 32) {
+    const int p = base + lane;
+    const bool valid = p < pairs;
+    float k0 = 0.f, k1 = 0.f, v0 = 0.f, v1 = 0.f;
+    if (valid) {
+      k0 = load_elem(kin, in_off + 2 * p, in_dt);
+      k1 = load_elem(kin, in_off + 2 * p + 1, in_dt);
+      v0 = load_elem(vin, in_off + 2 * p, in_dt);
+      v1 = load_elem(vin, in_off + 2 * p + 1, in_dt);
+      if (rope_row) rope_pair(k0, k1, rope_row[p], k0, k1);
+    }
+    const size_t e = static_cast<size_t>(dst) * hd + 2 * p;
+    if (c.dtype == kQ8_0) {
+      int8_t qk0, qk1, qv0, qv1;
+      __half sk, sv;
+      q8_0_pair(k0, k1, qk0, qk1, sk);
+      q8_0_pair(v0, v1, qv0, qv1, sv);
+      if (valid) {
+        *reinterpret_cast<char2*>(static_cast<int8_t*>(c.k) + e) = make_char2(qk0, qk1);
+        *reinterpret_cast<char2*>(static_cast<int8_t*>(c.v) + e) = make_char2(qv0, qv1);
+        if ((lane & 15) == 0) {
+          const size_t si = static_cast<size_t>(dst) * (hd / 32) + (2 * p) / 32;
+          c.k_scale[si] = __half_as_ushort(sk);
+          c.v_scale[si] = __half_as_ushort(sv);
+        }
+      }
+    } else if (valid) {
+      store_elem(c.k, e, c.dtype, k0);
+      store_elem(c.k, e + 1, c.dtype, k1);
+      store_elem(c.v, e, c.dtype, v0);
+      store_elem(c.v, e + 1, c.dtype, v1);
+    }
+  }
+}
+
+__device__ __forceinline__ float cache_value(const CacheView& c, const void* base,
+                                             const uint16_t* scale, int64_t row, int d) {
+  const size_t e = static_cast<size_t>(row) * c.hd + d;
+  if (c.dtype == kQ8_0) {
+    float s = __half2float(__ushort_as_half(scale[static_cast<size_t>(row) * (c.hd / 32) + d / 32]));
+    return s * static_cast<float>(static_cast<const int8_t*>(base)[e]);
+  }
+  return load_elem(base, e, c.dtype);
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- append --
+__global__ void __launch_bounds__(128) append_kernel(const __grid_constant__ AppendArgs a) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int hkv = a.cache.hkv;
+  const int rows = a.batch * a.new_len * hkv;
+  if (warp >= rows) return;
+  const int h = warp % hkv;
+  const int t = (warp / hkv) % a.new_len;
+  const int b = warp / (hkv * a.new_len);
+  const int pos = a.seqs.start[b] + t;
+  bool ok;
+  const int64_t dst = cache_row(a.cache, a.seqs.seq[b], pos, h, a.status, ok);
+  if (!ok) return;
+  const size_t in_off = (static_cast<size_t>(b * a.new_len + t) * hkv + h) * a.cache.hd;
+  const double2* rope = a.rope ? a.rope + static_cast<size_t>(pos) * (a.cache.hd / 2) : nullptr;
+  append_row(a.k, a.v, a.in_dtype, in_off, rope, a.cache, dst, lane);
+}
+
+cudaError_t launch_append(const AppendArgs& a, cudaStream_t s) {
+  const int rows = a.batch * a.new_len * a.cache.hkv;
+  if (rows == 0) return cudaSuccess;
+  const int blocks = (rows + 3) / 4;
+  append_kernel<<<blocks, 128, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- gather --
+__global__ void __launch_bounds__(128) gather_kernel(const __grid_constant__ GatherArgs a) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int hkv = a.cache.hkv, hd = a.cache.hd;
+  if (warp >= a.n * hkv) return;
+  const int i = warp / hkv, h = warp % hkv;
+  bool ok;
+  const int64_t row = cache_row(a.cache, a.seq, a.positions[i], h, nullptr, ok);
+  const size_t o = (static_cast<size_t>(i) * hkv + h) * hd;
+  for (int d = lane; d < hd; d += 32) {
+    a.k_out[o + d] = ok ? cache_value(a.cache, a.cache.k, a.cache.k_scale, row, d) : 0.f;
+    a.v_out[o + d] = ok ? cache_value(a.cache, a.cache.v, a.cache.v_scale, row, d) : 0.f;
+  }
+}
+
+cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s) {
+  const int rows = a.n * a.cache.hkv;
+  if (rows == 0) return cudaSuccess;
+  gather_kernel<<<(rows + 3) / 4, 128, 0, s>>>(a);
+  return cudaGetLastError();
+}
+
+// --------------------------------------------------------------- generic --
+// One CTA per (query head, query token).  Bit-level restatement of the
+// reference's per-head loop (layers.rs:434-445) on the GPU.
+__global__ void __launch_bounds__(256) generic_kernel(const __grid_constant__ AttnArgs a,
+                                                      int job0) {
+  const int h = blockIdx.x;
+  const int job = job0 + blockIdx.y;
+  const int b = job / a.new_len, t = job % a.new_len;
+  const int hd = a.cache.hd;
+  const int kvh = h / a.group;
+  const int qpos = a.seqs.start[b] + t;
+  const int L = qpos + 1;
+  const int seq = a.seqs.seq[b];
+  extern __shared__ float sh[];  // q [hd], reduction [32]
+  float* q = sh;
+  float* red = sh + hd;
+  const double2* rope_row = a.rope + static_cast<size_t>(qpos) * (hd / 2);
+  const size_t qoff = (static_cast<size_t>(job) * a.hq + h) * hd;
+  for (int p = threadIdx.x; p < hd / 2; p += blockDim.x) {
+    float y0, y1;
+    rope_pair(load_elem(a.q, qoff + 2 * p, a.in_dtype), load_elem(a.q, qoff + 2 * p + 1, a.in_dtype),
+              rope_row[p], y0, y1);
+    q[2 * p] = y0;
+    q[2 * p + 1] = y1;
+  }
+  __syncthreads();
+  const size_t srow = (static_cast<size_t>(blockIdx.y) * a.hq + h) * a.max_len;
+  float* sc = a.scratch + srow;
+  double* cd = a.scratch_d + srow;
+  // scores, scaled (matmul then scale, ops.rs:63-94 and :257-261)
+  float mx = -CUDART_INF_F;
+  for (int j = threadIdx.x; j < L; j += blockDim.x) {
+    bool ok;
+    const int64_t row = cache_row(a.cache, seq, j, kvh, a.status, ok);
+    float acc = 0.f;
+    for (int d = 0; d < hd; ++d)
+      acc = __fadd_rn(acc, __fmul_rn(q[d], ok ? cache_value(a.cache, a.cache.k, a.cache.k_scale,
+                                                               row, d)
+                                               : 0.f));
+    acc = __fmul_rn(acc, a.scale);
+    sc[j] = acc;
+    mx = fmaxf(mx, acc);
+  }
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : -CUDART_INF_F;
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  mx = red[0];
+  // contributions in f64 (ops.rs:298-310)
+  for (int j = threadIdx.x; j < L; j += blockDim.x) {
+    const float v = sc[j];
+    double c;
+    if (mx == -CUDART_INF_F) c = 1.0;
+    else if (mx == CUDART_INF_F) c = (v == CUDART_INF_F) ? 1.0 : 0.0;
+    else c = exp(static_cast<double>(v) - static_cast<double>(mx));
+    cd[j] = c;
+  }
+  __syncthreads();
+  __shared__ double denom_s;
+  if (threadIdx.x == 0) {
+    double den = 0.0;
+    for (int j = 0; j < L; ++j) den += cd[j];  // sequential, as the reference sums
+    denom_s = den;
+  }
+  __syncthreads();
+  const double den = denom_s;
+  for (int j = threadIdx.x; j < L; j += blockDim.x) sc[j] = static_cast<float>(cd[j] / den);
+  __syncthreads();
+  // P.V, sequential over keys (ops.rs:81-91 i-k-j order)
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < L; ++j) {
+      bool ok;
+      const int64_t row = cache_row(a.cache, seq, j, kvh, nullptr, ok);
+      const float vv = ok ? cache_value(a.cache, a.cache.v, a.cache.v_scale, row, d) : 0.f;
+      acc = __fadd_rn(acc, __fmul_rn(sc[j], vv));
+    }
+    store_elem(a.out, (static_cast<size_t>(job) * a.hq + h) * hd + d, a.out_dtype, acc);
+  }
+}
+
+cudaError_t launch_generic(const AttnArgs& a, cudaStream_t s) {
+  const int jobs = a.batch * a.new_len;
+  const size_t smem = (a.cache.hd + 32) * sizeof(float);
+  for (int j0 = 0; j0 < jobs; j0 += 65535) {
+    dim3 grid(a.hq, min(65535, jobs - j0));
+    generic_kernel<<<grid, 256, smem, s>>>(a, j0);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// ---------------------------------------------------------------- splitkv --
+namespace {
+
+template <int HD, int DT>
+struct SplitCfg {
+  static constexpr bool kQ8 = DT == kQ8_0;
+  static constexpr bool kBF = DT == kBF16;
+  // K and V tile bytes of one 64-position stage
+  static constexpr int kKBytes = kQ8 ? kTile * HD : kTile * HD * 2;
+  static constexpr int kScaleBytes = kQ8 ? kTile * (HD / 32) * 2 : 0;
+  static constexpr int kRaw = 2 * kKBytes + 2 * kScaleBytes;
+  static constexpr int kStageBytes = (kRaw + 1023) / 1024 * 1024;
+  static constexpr int kStages = kQ8 ? 5 : (HD == 128 ? 3 : 6);
+  static constexpr int kTx = kRaw;
+  static constexpr int kQLd = HD + 8;  // q tile row stride (elements), padded
+  static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes +
+                                  16 * kQLd * 2 + 64 * sizeof(float) + 16 +
+                                  2 * kStages * sizeof(uint64_t);
+  static_assert(4 * 8 * HD * 4 <= kStages * kStageBytes, "merge buffer must fit the stages");
+};
+
+// Logical MMA k index of physical head-dim element d for int8 K rows: a
+// thread's four values of one k-step sit in 4 consecutive bytes, so one
+// 32-bit shared load feeds its B fragment, and each 16-wide k-step stays
+// inside one 32-element Q8_0 block.
+__device__ __forceinline__ int q8_logical_k(int d) {
+  const int blk = d >> 5, s = (d >> 4) & 1, t = (d >> 2) & 3, e = d & 3;
+  return blk * 32 + s * 16 + (e < 2 ? 2 * t + e : 2 * t + 6 + e);
+}
+
+__device__ __forceinline__ uint32_t swz128(int row, int chunk) {
+  // byte offset of 16-byte chunk `chunk` (0..7) of row `row` in a 128B-swizzled box
+  return static_cast<uint32_t>(row * 128 + (((chunk ^ (row & 7))) << 4));
+}
+
+__device__ __forceinline__ void bar_consumers() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+}  // namespace
+
+template <int HD, int DT>
+__global__ void __launch_bounds__(160, 2)
+    splitkv_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ CUtensorMap kmap,
+                   const __grid_constant__ CUtensorMap vmap, int job0) {
+  using C = SplitCfg<HD, DT>;
+  constexpr bool Q8 = C::kQ8;
+  constexpr bool BF = C::kBF;  // bf16 operands for both MMAs; f16 otherwise
+  constexpr int NKS = HD / 16;  // k-steps of QK^T
+  constexpr int NO = HD / 8;    // n-tiles of the output
+
+  const int split = blockIdx.x, kvh = blockIdx.y, job = job0 + blockIdx.z;
+  const int b = job / a.new_len, t_tok = job % a.new_len;
+  const int seq = a.seqs.seq[b];
+  const int qpos = a.seqs.start[b] + t_tok;
+  const int L = qpos + 1;
+  const int ntiles = (L + kTile - 1) / kTile;
+  const int nsplit = (ntiles + a.tiles_per_split - 1) / a.tiles_per_split;
+  if (split >= nsplit) return;
+  const int tile0 = split * a.tiles_per_split;
+  const int my_tiles = min(ntiles, tile0 + a.tiles_per_split) - tile0;
+  const int hkv = a.cache.hkv;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* stages = smem;
+  uint16_t* qs = reinterpret_cast<uint16_t*>(smem + C::kStages * C::kStageBytes);
+  float* ml = reinterpret_cast<float*>(qs + 16 * C::kQLd);
+  int* flag = reinterpret_cast<int*>(ml + 64);
+  uint64_t* full = reinterpret_cast<uint64_t*>(flag + 4);
+  uint64_t* empty = full + C::kStages;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 4);
+    }
+    fence_mbar_init();
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+
+  const double2* rope_row = a.rope + static_cast<size_t>(qpos) * (HD / 2);
+  if (warp < 4) {
+    // Rotated query rows of this KV head's group, split hi/lo: row g holds the
+    // high part of head g, row g+8 the remainder.
+    for (int idx = threadIdx.x; idx < 8 * (HD / 2); idx += 128) {
+      const int hg = idx / (HD / 2), p = idx % (HD / 2);
+      float y0 = 0.f, y1 = 0.f;
+      if (hg < a.group) {
+        const size_t off = (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + 2 * p;
+        rope_pair(load_elem(a.q, off, a.in_dtype), load_elem(a.q, off + 1, a.in_dtype),
+                  rope_row[p], y0, y1);
+      }
+      float h0, l0, h1, l1;
+      split16<BF>(y0, h0, l0);
+      split16<BF>(y1, h1, l1);
+      const int k0 = Q8 ? q8_logical_k(2 * p) : 2 * p;
+      const int k1 = Q8 ? q8_logical_k(2 * p + 1) : 2 * p + 1;
+      const uint32_t hh = pack2<BF>(h0, h1), ll = pack2<BF>(l0, l1);
+      qs[hg * C::kQLd + k0] = static_cast<uint16_t>(hh & 0xffff);
+      qs[hg * C::kQLd + k1] = static_cast<uint16_t>(hh >> 16);
+      qs[(hg + 8) * C::kQLd + k0] = static_cast<uint16_t>(ll & 0xffff);
+      qs[(hg + 8) * C::kQLd + k1] = static_cast<uint16_t>(ll >> 16);
+    }
+    // Single-token decode: the CTA holding the last tile writes the new K/V.
+    if (a.fuse_append && split == nsplit - 1 && warp == 0) {
+      bool ok;
+      const int64_t dst = cache_row(a.cache, seq, qpos, kvh, a.status, ok);
+      if (ok)
+        append_row(a.k, a.v, a.in_dtype, (static_cast<size_t>(job) * hkv + kvh) * HD, rope_row,
+                   a.cache, dst, lane);
+      fence_proxy_async_global();
+    }
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------ producer --
+  if (warp == 4) {
+    if (lane == 0) {
+      const int* bt = a.cache.block_table + static_cast<size_t>(seq) * a.cache.pages_per_seq;
+      for (int i = 0; i < my_tiles; ++i) {
+        const int st = i % C::kStages;
+        if (i >= C::kStages && !mbar_wait(&empty[st], ((i / C::kStages) - 1) & 1, a.status))
+          break;
+        const int p0 = (tile0 + i) * kTile;
+        int page = bt[p0 / a.cache.page];
+        if (page < 0 || page >= a.cache.num_pages) {
+          atomicOr(a.status, kStatusBadPage);
+          page = 0;  // keep the pipeline consistent; the result is flagged
+        }
+        const int row = (page * hkv + kvh) * a.cache.page + p0 % a.cache.page;
+        uint8_t* sb = stages + st * C::kStageBytes;
+        mbar_arrive_expect_tx(&full[st], C::kTx);
+        if constexpr (Q8) {
+          tma_load_2d(sb, &kmap, 0, row, &full[st]);
+          tma_load_2d(sb + C::kKBytes, &vmap, 0, row, &full[st]);
+          bulk_load(sb + 2 * C::kKBytes, a.cache.k_scale + static_cast<size_t>(row) * (HD / 32),
+                    C::kScaleBytes, &full[st]);
+          bulk_load(sb + 2 * C::kKBytes + C::kScaleBytes,
+                    a.cache.v_scale + static_cast<size_t>(row) * (HD / 32), C::kScaleBytes,
+                    &full[st]);
+        } else {
+#pragma unroll
+          for (int box = 0; box < HD / 64; ++box) {
+            tma_load_2d(sb + box * 8192, &kmap, box * 64, row, &full[st]);
+            tma_load_2d(sb + C::kKBytes + box * 8192, &vmap, box * 64, row, &full[st]);
+          }
+        }
+      }
+    }
+    return;
+  }
+
+  // ----------------------------------------------------------- consumers --
+  uint32_t qa[NKS][4];
+#pragma unroll
+  for (int ks = 0; ks < NKS; ++ks) {
+    const int r = ((lane >> 3) & 1) * 8 + (lane & 7);
+    const int col = ks * 16 + (lane >> 4) * 8;
+    ldmatrix_x4(smem_u32(qs + r * C::kQLd + col), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+  }
+
+  float o[NO][4];
+#pragma unroll
+  for (int j = 0; j < NO; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m = -CUDART_INF_F, l = 0.f;
+  const float sl2 = a.scale * kLog2e;
+
+  for (int i = 0; i < my_tiles; ++i) {
+    const int st = i % C::kStages;
+    const bool ok = mbar_wait(&full[st], (i / C::kStages) & 1, a.status);
+    if (__any_sync(0xffffffffu, !ok)) break;
+    uint8_t* sb = stages + st * C::kStageBytes;
+    const int valid = L - (tile0 + i) * kTile - 16 * warp;  // live positions in my 16-row slice
+    if (valid > 0) {
+      if (valid < 16) {
+        // Rows past the sequence end hold stale data; zero their V so that
+        // 0 * stale never reaches the accumulators.
+        if constexpr (Q8) {
+          uint16_t* vsc = reinterpret_cast<uint16_t*>(sb + 2 * C::kKBytes + C::kScaleBytes);
+          for (int r = valid + lane / (HD / 32); r < 16; r += 32 / (HD / 32))
+            vsc[(16 * warp + r) * (HD / 32) + lane % (HD / 32)] = 0;
+        } else {
+          for (int idx = lane; idx < (16 - valid) * (HD / 8); idx += 32) {
+            const int r = 16 * warp + valid + idx / (HD / 8), c = idx % (HD / 8);
+            *reinterpret_cast<uint4*>(sb + C::kKBytes + (c >> 3) * 8192 + swz128(r, c & 7)) =
+                make_uint4(0, 0, 0, 0);
+          }
+        }
+        __syncwarp();
+      }
+      // ---- S = Q K^T over this warp's 16 positions (two n-tiles of 8)
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      if constexpr (Q8) {
+        const uint16_t* ksc = reinterpret_cast<const uint16_t*>(sb + 2 * C::kKBytes);
+#pragma unroll
+        for (int blk = 0; blk < HD / 32; ++blk) {
+          float sb2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+          for (int s2 = 0; s2 < 2; ++s2) {
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+              const int r = 16 * warp + 8 * nt + g;
+              const int byte = 32 * blk + 16 * s2 + 4 * tq;
+              const uint32_t w =
+                  *reinterpret_cast<const uint32_t*>(sb + swz128(r, byte >> 4) + (byte & 15));
+              uint32_t b0, b1;
+              i8x4_to_h2x2(w, b0, b1);
+              mma16816<false>(sb2[nt], qa[2 * blk + s2], b0, b1);
+            }
+          }
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int r0 = 16 * warp + 8 * nt + 2 * tq;
+            const float d0 = __half2float(__ushort_as_half(ksc[r0 * (HD / 32) + blk]));
+            const float d1 = __half2float(__ushort_as_half(ksc[(r0 + 1) * (HD / 32) + blk]));
+            s[nt][0] += d0 * sb2[nt][0];
+            s[nt][1] += d1 * sb2[nt][1];
+            s[nt][2] += d0 * sb2[nt][2];
+            s[nt][3] += d1 * sb2[nt][3];
+          }
+        }
+      } else {
+        const uint32_t kbase = smem_u32(sb);
+#pragma unroll
+        for (int ks = 0; ks < NKS; ++ks) {
+          const int r = 16 * warp + (lane >> 4) * 8 + (lane & 7);
+          const int c = 2 * ks + ((lane >> 3) & 1);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(kbase + (c >> 3) * 8192 + swz128(r, c & 7), b0, b1, b2, b3);
+          mma16816<BF>(s[0], qa[ks], b0, b1);
+          mma16816<BF>(s[1], qa[ks], b2, b3);
+        }
+      }
+      // ---- online softmax for head g over positions 2tq, 2tq+1, 8+2tq, 9+2tq
+      float x[4] = {s[0][0] + s[0][2], s[0][1] + s[0][3], s[1][0] + s[1][2], s[1][1] + s[1][3]};
+      const int pp[4] = {2 * tq, 2 * tq + 1, 8 + 2 * tq, 9 + 2 * tq};
+      float mx = -CUDART_INF_F;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        x[e] = pp[e] < valid ? x[e] * sl2 : -CUDART_INF_F;
+        mx = fmaxf(mx, x[e]);
+      }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m, mx);
+      const float base = m_new == -CUDART_INF_F ? 0.f : m_new;
+      const float corr = exp2f(m - base);
+      float p[4], psum = 0.f;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        p[e] = exp2f(x[e] - base);
+        psum += p[e];
+      }
+      l = l * corr + psum;
+      m = m_new;
+#pragma unroll
+      for (int j = 0; j < NO; ++j) {
+        o[j][0] *= corr;
+        o[j][1] *= corr;
+        o[j][2] *= corr;
+        o[j][3] *= corr;
+      }
+      // P as the A operand: row g = high part, row g+8 = remainder.
+      constexpr bool PBF = BF;  // Q8_0 dequantises V to f16
+      float ph[4], pl[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) split16<PBF>(p[e], ph[e], pl[e]);
+      const uint32_t pa[4] = {pack2<PBF>(ph[0], ph[1]), pack2<PBF>(pl[0], pl[1]),
+                              pack2<PBF>(ph[2], ph[3]), pack2<PBF>(pl[2], pl[3])};
+      // ---- O += P V
+      if constexpr (Q8) {
+        const uint8_t* vq = sb + C::kKBytes;
+        const uint16_t* vsc =
+            reinterpret_cast<const uint16_t*>(sb + 2 * C::kKBytes + C::kScaleBytes);
+        const int rA = 16 * warp + 2 * tq;
+        const uint4 A = *reinterpret_cast<const uint4*>(vq + swz128(rA, g));
+        const uint4 B = *reinterpret_cast<const uint4*>(vq + swz128(rA + 1, g));
+        const uint4 Cq = *reinterpret_cast<const uint4*>(vq + swz128(rA + 8, g));
+        const uint4 D = *reinterpret_cast<const uint4*>(vq + swz128(rA + 9, g));
+        const int sbk = g >> 1;  // this thread's 16 columns lie in Q8_0 block g/2
+        const __half2 dAB = __halves2half2(__ushort_as_half(vsc[rA * (HD / 32) + sbk]),
+                                           __ushort_as_half(vsc[(rA + 1) * (HD / 32) + sbk]));
+        const __half2 dCD = __halves2half2(__ushort_as_half(vsc[(rA + 8) * (HD / 32) + sbk]),
+                                           __ushort_as_half(vsc[(rA + 9) * (HD / 32) + sbk]));
+        const uint32_t aw[4] = {A.x, A.y, A.z, A.w}, bw[4] = {B.x, B.y, B.z, B.w};
+        const uint32_t cw[4] = {Cq.x, Cq.y, Cq.z, Cq.w}, dw[4] = {D.x, D.y, D.z, D.w};
+#pragma unroll
+        for (int w4 = 0; w4 < 4; ++w4) {
+          uint32_t ab01, ab23, cd01, cd23;
+          asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(ab01) : "r"(aw[w4]), "r"(bw[w4]));
+          asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(ab23) : "r"(aw[w4]), "r"(bw[w4]));
+          asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(cd01) : "r"(cw[w4]), "r"(dw[w4]));
+          asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(cd23) : "r"(cw[w4]), "r"(dw[w4]));
+          uint32_t x0, x1, x2, x3, y0, y1, y2, y3;
+          i8x4_to_h2x2(ab01, x0, x1);
+          i8x4_to_h2x2(ab23, x2, x3);
+          i8x4_to_h2x2(cd01, y0, y1);
+          i8x4_to_h2x2(cd23, y2, y3);
+          const uint32_t xs[4] = {x0, x1, x2, x3}, ys[4] = {y0, y1, y2, y3};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __half2 bx = __hmul2(*reinterpret_cast<const __half2*>(&xs[e]), dAB);
+            __half2 by = __hmul2(*reinterpret_cast<const __half2*>(&ys[e]), dCD);
+            mma16816<false>(o[4 * w4 + e], pa, *reinterpret_cast<uint32_t*>(&bx),
+                            *reinterpret_cast<uint32_t*>(&by));
+          }
+        }
+      } else {
+        const uint32_t vbase = smem_u32(sb + C::kKBytes);
+#pragma unroll
+        for (int jj = 0; jj < HD / 16; ++jj) {
+          const int r = 16 * warp + ((lane >> 3) & 1) * 8 + (lane & 7);
+          const int c = 2 * jj + (lane >> 4);
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4_trans(vbase + (c >> 3) * 8192 + swz128(r, c & 7), b0, b1, b2, b3);
+          mma16816<BF>(o[2 * jj], pa, b0, b1);
+          mma16816<BF>(o[2 * jj + 1], pa, b2, b3);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+  }
+
+  // ------------------------------------------------------------- epilogue --
+  l += __shfl_xor_sync(0xffffffffu, l, 1);
+  l += __shfl_xor_sync(0xffffffffu, l, 2);
+  bar_consumers();  // every consumer is done reading the stages
+  if (tq == 0) {
+    ml[(warp * 8 + g) * 2] = m;
+    ml[(warp * 8 + g) * 2 + 1] = l;
+  }
+  bar_consumers();
+  float M = -CUDART_INF_F;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) M = fmaxf(M, ml[(w * 8 + g) * 2]);
+  const float Mb = M == -CUDART_INF_F ? 0.f : M;
+  const float f = exp2f(m - Mb);
+  float* ob = reinterpret_cast<float*>(stages);  // [4 warps][8 heads][HD]
+#pragma unroll
+  for (int j = 0; j < NO; ++j) {
+    // Q8_0 columns were permuted: n-tile j, column n -> head-dim 16n + j.
+    const int c0 = Q8 ? 16 * (2 * tq) + j : 8 * j + 2 * tq;
+    const int c1 = Q8 ? 16 * (2 * tq + 1) + j : 8 * j + 2 * tq + 1;
+    ob[(warp * 8 + g) * HD + c0] = (o[j][0] + o[j][2]) * f;
+    ob[(warp * 8 + g) * HD + c1] = (o[j][1] + o[j][3]) * f;
+  }
+  bar_consumers();
+  const int tid = threadIdx.x;
+  const size_t pslot = (static_cast<size_t>(job) * hkv + kvh) * a.max_splits;
+  for (int idx = tid; idx < a.group * HD; idx += 128) {
+    const int hg = idx / HD, d = idx % HD;
+    float Mh = -CUDART_INF_F;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) Mh = fmaxf(Mh, ml[(w * 8 + hg) * 2]);
+    const float Mhb = Mh == -CUDART_INF_F ? 0.f : Mh;
+    float Lh = 0.f, sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      Lh += ml[(w * 8 + hg) * 2 + 1] * exp2f(ml[(w * 8 + hg) * 2] - Mhb);
+      sum += ob[(w * 8 + hg) * HD + d];
+    }
+    if (nsplit == 1) {
+      store_elem(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d,
+                 a.out_dtype, sum / Lh);
+    } else {
+      a.part_o[((pslot + split) * 8 + hg) * HD + d] = sum / Lh;
+      if (d == 0) {
+        a.part_ml[((pslot + split) * 8 + hg) * 2] = Mh;
+        a.part_ml[((pslot + split) * 8 + hg) * 2 + 1] = Lh;
+      }
+    }
+  }
+  if (nsplit == 1) return;
+  // ---- the last CTA of this (job, kv head) merges the splits
+  __threadfence();
+  bar_consumers();
+  if (tid == 0) {
+    const int prev = atomicAdd(&a.counters[static_cast<size_t>(job) * hkv + kvh], 1);
+    flag[0] = prev == nsplit - 1;
+  }
+  bar_consumers();
+  if (!flag[0]) return;
+  __threadfence();
+  for (int idx = tid; idx < a.group * HD; idx += 128) {
+    const int hg = idx / HD, d = idx % HD;
+    float Mx = -CUDART_INF_F;
+    for (int s = 0; s < nsplit; ++s)
+      Mx = fmaxf(Mx, __ldcg(&a.part_ml[((pslot + s) * 8 + hg) * 2]));
+    const float Mxb = Mx == -CUDART_INF_F ? 0.f : Mx;
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float w = __ldcg(&a.part_ml[((pslot + s) * 8 + hg) * 2 + 1]) *
+                      exp2f(__ldcg(&a.part_ml[((pslot + s) * 8 + hg) * 2]) - Mxb);
+      num += w * __ldcg(&a.part_o[((pslot + s) * 8 + hg) * HD + d]);
+      den += w;
+    }
+    store_elem(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d,
+               a.out_dtype, num / den);
+  }
+  if (tid == 0) a.counters[static_cast<size_t>(job) * hkv + kvh] = 0;
+}
+
+size_t splitkv_smem_bytes(int hd, int dtype) {
+  if (dtype == kQ8_0) return SplitCfg<128, kQ8_0>::kSmem;
+  if (hd == 128) return dtype == kBF16 ? SplitCfg<128, kBF16>::kSmem : SplitCfg<128, kF16>::kSmem;
+  return dtype == kBF16 ? SplitCfg<64, kBF16>::kSmem : SplitCfg<64, kF16>::kSmem;
+}
+
+bool splitkv_supported(int hd, int dtype, int group, int page) {
+  if (group < 1 || group > 8 || page % kTile != 0) return false;
+  if (dtype == kQ8_0) return hd == 128;
+  return (dtype == kF16 || dtype == kBF16) && (hd == 64 || hd == 128);
+}
+
+template <int HD, int DT>
+static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
+                                    const CUtensorMap* vmap, int jobs, cudaStream_t s) {
+  using C = SplitCfg<HD, DT>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(splitkv_kernel<HD, DT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(C::kSmem));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  for (int j0 = 0; j0 < jobs; j0 += 65535) {
+    dim3 grid(a.max_splits, a.cache.hkv, min(65535, jobs - j0));
+    splitkv_kernel<HD, DT><<<grid, 160, C::kSmem, s>>>(a, *kmap, *vmap, j0);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+cudaError_t launch_splitkv(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,
+                           int jobs, cudaStream_t s) {
+  const int hd = a.cache.hd, dt = a.cache.dtype;
+  if (dt == kQ8_0) return launch_splitkv_t<128, kQ8_0>(a, kmap, vmap, jobs, s);
+  if (hd == 128)
+    return dt == kBF16 ? launch_splitkv_t<128, kBF16>(a, kmap, vmap, jobs, s)
+                       : launch_splitkv_t<128, kF16>(a, kmap, vmap, jobs, s);
+  return dt == kBF16 ? launch_splitkv_t<64, kBF16>(a, kmap, vmap, jobs, s)
+                     : launch_splitkv_t<64, kF16>(a, kmap, vmap, jobs, s);
+}
+
+}  // namespace ql

@@ -1,0 +1,97 @@
+// ql_kernels.cuh -- launch interfaces of the attention kernels (host + device).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ql {
+
+// Sequences one launch can carry in its parameter block.
+constexpr int kMaxBatch = 256;
+// Positions per KV tile of the split-KV kernels; pages hold a multiple of it.
+constexpr int kTile = 64;
+
+// Per-call sequence table, passed by value in the kernel parameters.
+struct SeqTable {
+  int32_t seq[kMaxBatch];    // cache slot
+  int32_t start[kMaxBatch];  // position of the first new token
+};
+
+// Geometry and storage of one layer of the paged KV cache.
+struct CacheView {
+  void* k;               // K values: [pages][hkv][page][hd] (int8 for Q8_0)
+  void* v;               // V values, same geometry
+  uint16_t* k_scale;     // Q8_0 only: [pages][hkv][page][hd/32] f16 bits
+  uint16_t* v_scale;
+  const int32_t* block_table;  // [max_batch][pages_per_seq]
+  int32_t pages_per_seq;
+  int32_t num_pages;
+  int32_t page;          // positions per page
+  int32_t hkv;
+  int32_t hd;
+  int32_t dtype;         // kF32 / kF16 / kBF16 / kQ8_0
+};
+
+// Appends new K (rotated unless rope == nullptr) and V rows into the cache.
+struct AppendArgs {
+  const void* k;
+  const void* v;
+  int32_t in_dtype;
+  int32_t batch;
+  int32_t new_len;
+  const double2* rope;  // [max_seq][hd/2] (cos, sin) or nullptr
+  CacheView cache;
+  uint32_t* status;
+  SeqTable seqs;
+};
+
+// Attention of `new_len` query tokens per sequence over the cached prefix.
+struct AttnArgs {
+  const void* q;  // [batch, new_len, hq, hd] pre-RoPE
+  const void* k;  // new K/V, used when fuse_append (new_len == 1)
+  const void* v;
+  int32_t in_dtype;
+  void* out;  // [batch, new_len, hq*hd]
+  int32_t out_dtype;
+  const double2* rope;
+  CacheView cache;
+  int32_t hq;
+  int32_t group;  // hq / hkv
+  int32_t batch;
+  int32_t new_len;
+  float scale;       // 1/sqrt(hd), computed as the reference does
+  int32_t fuse_append;
+  int32_t tiles_per_split;
+  int32_t max_splits;
+  float* part_o;     // [jobs][hkv][max_splits][8][hd]
+  float* part_ml;    // [jobs][hkv][max_splits][8][2]
+  int32_t* counters; // [jobs][hkv], zero between launches
+  float* scratch;    // generic kernel: scores / probabilities
+  double* scratch_d; // generic kernel: f64 contributions
+  int32_t max_len;   // generic kernel: scratch row length
+  uint32_t* status;
+  SeqTable seqs;
+};
+
+struct GatherArgs {
+  const int32_t* positions;  // device [n]
+  int32_t n;
+  int32_t seq;
+  float* k_out;
+  float* v_out;
+  CacheView cache;
+};
+
+// Dynamic shared memory the split-KV kernel needs for a configuration.
+size_t splitkv_smem_bytes(int hd, int dtype);
+// Whether the split-KV tensor-core kernel handles this configuration.
+bool splitkv_supported(int hd, int dtype, int group, int page);
+
+cudaError_t launch_append(const AppendArgs& a, cudaStream_t s);
+cudaError_t launch_splitkv(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,
+                           int grid_jobs, cudaStream_t s);
+cudaError_t launch_generic(const AttnArgs& a, cudaStream_t s);
+cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s);
+
+}  // namespace ql
