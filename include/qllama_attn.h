@@ -157,6 +157,37 @@ typedef struct {
 
 int ql_attn_forward(ql_ctx* ctx, ql_kv* kv, const ql_attn_args* args);
 
+/* ---- single-token decode that allocates nothing ----------------------------
+ * No counterpart in the reference; an addition for callers that must not
+ * allocate device memory while they serve, such as a host runtime that hands
+ * the GPU's memory to its own allocator at start-up, or a serving loop that
+ * promises no cudaMalloc/cudaFree between warm-up and shutdown.
+ *
+ * It decodes one token per sequence like ql_attn_forward (RoPE, fused append,
+ * causal GQA attention), but keeps its scratch (split partials and merge
+ * counters) in one static device array of QL_NOALLOC_SCRATCH_BYTES that every
+ * GPU loading the library holds until the process exits.  It calls no
+ * cudaMalloc, cudaFree or allocating library routine.  The cache itself is
+ * allocated earlier, by ql_kv_create.
+ *
+ * Limits (rejected with QL_ERR_INVALID or QL_ERR_UNSUPPORTED and a message):
+ * new_len must be 1; q/k/v/out must be device memory (QL_MEM_DEVICE); the
+ * cache must be f16 or bf16 with head_dim 64 or 128, or Q8_0 with head_dim
+ * 128, with at most 8 query heads per KV head; batch*num_kv_heads must not
+ * exceed QL_NOALLOC_MAX_PAIRS.  When the partials would not fit the array,
+ * fewer KV splits are used.  RoPE angles are evaluated on the device in f64,
+ * so results can differ from ql_attn_forward in the last bits.
+ *
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * Every call shares the array and each call clears its counters, so calls
+ * that overlap on the GPU (other streams or contexts on the same device)
+ * race and corrupt each other's results: serialise them.
+ */
+#define QL_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+#define QL_NOALLOC_MAX_PAIRS 16384
+int ql_attn_decode_noalloc(ql_ctx* ctx, ql_kv* kv, const ql_attn_args* args);
+
 #ifdef __cplusplus
 }
 #endif

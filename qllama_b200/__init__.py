@@ -33,6 +33,7 @@ EXPORTS = (
     "ql_version", "ql_last_error", "ql_ctx_create", "ql_ctx_destroy", "ql_ctx_set_stream",
     "ql_ctx_synchronize", "ql_kv_create", "ql_kv_destroy", "ql_kv_clear", "ql_kv_clear_seq",
     "ql_kv_seq_len", "ql_kv_layer_len", "ql_kv_update", "ql_kv_get", "ql_attn_forward",
+    "ql_attn_decode_noalloc",
 )
 
 
@@ -98,6 +99,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
                                i32]
     L.ql_kv_get.argtypes = [vp, vp, i32, i32, i32p, i64, vp, vp, i32]
     L.ql_attn_forward.argtypes = [vp, vp, ctypes.POINTER(AttnArgs)]
+    L.ql_attn_decode_noalloc.argtypes = [vp, vp, ctypes.POINTER(AttnArgs)]
     for name in EXPORTS:
         if name not in ("ql_version", "ql_last_error"):
             getattr(L, name).restype = ctypes.c_int

@@ -254,6 +254,40 @@ int check_status(ql_ctx* c) {
 
 }  // namespace
 
+// ---------------------------------------------------- no-allocation decode --
+// Fixed device scratch for ql_attn_decode_noalloc: the merge counters, then
+// the split partials (m, l) and O.  Every GPU that loads this library holds
+// it until the process exits; it starts zeroed and every call clears the
+// counters again before use.  In host code `g_noalloc_scratch` is only a
+// stand-in symbol: kernels get the device address from cudaGetSymbolAddress.
+namespace {
+
+constexpr size_t kNoAllocBytes = QL_NOALLOC_SCRATCH_BYTES;
+constexpr int kNoAllocPairs = QL_NOALLOC_MAX_PAIRS;
+constexpr size_t kNoAllocCounterBytes = static_cast<size_t>(kNoAllocPairs) * sizeof(int32_t);
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+char* g_noalloc_addr[kMaxDevices] = {};  // device address of the array, per device
+
+// Called with `device` current.  The lookup runs once per device.
+int noalloc_scratch(int device, char** out) {
+  if (device < 0 || device >= kMaxDevices)
+    return fail(QL_ERR_UNSUPPORTED, "device %d is beyond the %d devices the scratch table covers",
+                device, kMaxDevices);
+  if (!g_noalloc_addr[device]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "look up the no-allocation scratch");
+    g_noalloc_addr[device] = static_cast<char*>(p);
+  }
+  *out = g_noalloc_addr[device];
+  return QL_OK;
+}
+
+}  // namespace
+
 extern "C" {
 
 const char* ql_version(void) { return "qllama_b200 0.1 (sm_100a)"; }
@@ -766,4 +800,138 @@ int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   return QL_OK;
 }
 
+int ql_attn_decode_noalloc(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
+  if (!c || !kv || !a) return fail(QL_ERR_INVALID, "ql_attn_decode_noalloc: NULL argument");
+  const int hq = a->num_heads, hkv = a->num_kv_heads, hd = a->head_dim;
+  if (hq <= 0 || hkv <= 0 || hd <= 0)
+    return fail(QL_ERR_INVALID, "Attention head counts and head_dim must be positive");
+  if (hq % hkv != 0)
+    return fail(QL_ERR_INVALID, "num_heads %d must be divisible by num_kv_heads %d", hq, hkv);
+  if (a->new_len != 1)
+    return fail(QL_ERR_INVALID, "ql_attn_decode_noalloc decodes one token per sequence "
+                "(new_len 1), got new_len %d", a->new_len);
+  if (a->mem != QL_MEM_DEVICE)
+    return fail(QL_ERR_INVALID, "ql_attn_decode_noalloc takes device buffers only "
+                "(host staging would need an allocation)");
+  if (a->batch < 1 || a->batch > ql::kMaxBatch || a->batch > kv->cfg.max_batch)
+    return fail(QL_ERR_INVALID, "batch %d is outside 1..%d (%d cache slots)", a->batch,
+                ql::kMaxBatch, kv->cfg.max_batch);
+  if (static_cast<long long>(a->batch) * hkv > kNoAllocPairs)
+    return fail(QL_ERR_INVALID, "batch*num_kv_heads = %lld exceeds the no-allocation limit of %d "
+                "(sequence, KV head) pairs", static_cast<long long>(a->batch) * hkv,
+                kNoAllocPairs);
+  if (!a->seq_ids || !a->start_pos || !a->q || !a->k || !a->v || !a->out)
+    return fail(QL_ERR_INVALID, "ql_attn_decode_noalloc: NULL buffer");
+  if ((hd & 1) != 0)
+    return fail(QL_ERR_INVALID,
+                "RoPE requires shape [seq_len, ..., head_dim] with a positive even head_dim");
+  if (!std::isfinite(a->rope_theta) || a->rope_theta <= 0.f)
+    return fail(QL_ERR_INVALID, "RoPE theta must be finite and positive");
+  if (!valid_io_dtype(a->in_dtype) || !valid_io_dtype(a->out_dtype))
+    return fail(QL_ERR_INVALID, "unknown input/output dtype (%d, %d)", a->in_dtype, a->out_dtype);
+  const int layer = a->layer_idx;
+  if (layer < 0 || layer >= kv->cfg.num_layers)
+    return fail(QL_ERR_INVALID, "KV cache layer index %d out of range (cache has %d layers)",
+                layer, kv->cfg.num_layers);
+  if (hkv != kv->cfg.num_kv_heads || hd != kv->cfg.head_dim)
+    return fail(QL_ERR_INVALID, "K shape [1, %d, %d] does not match cache [_, %d, %d]", hkv, hd,
+                kv->cfg.num_kv_heads, kv->cfg.head_dim);
+  const int group = hq / hkv;
+  if (!kv->have_maps || !ql::splitkv_supported(hd, kv->cfg.dtype, group, kv->cfg.page_size))
+    return fail(QL_ERR_UNSUPPORTED, "ql_attn_decode_noalloc needs an f16/bf16 cache with head_dim "
+                "64 or 128 or a Q8_0 cache with head_dim 128, and at most 8 query heads per KV "
+                "head");
+  std::vector<int32_t> seqs(a->batch);
+  std::vector<int64_t> ends(a->batch);
+  std::vector<char> seen(kv->cfg.max_batch, 0);
+  int max_tiles = 0;
+  long long total_tiles = 0;
+  for (int b = 0; b < a->batch; ++b) {
+    const int s = a->seq_ids[b];
+    if (s < 0 || s >= kv->cfg.max_batch)
+      return fail(QL_ERR_INVALID, "sequence %d out of range (cache has %d slots)", s,
+                  kv->cfg.max_batch);
+    if (seen[s]) return fail(QL_ERR_INVALID, "sequence %d appears twice in one call", s);
+    seen[s] = 1;
+    const int64_t start = a->start_pos[b], cur = len_at(kv, layer, s);
+    if (start < 0) return fail(QL_ERR_INVALID, "start_pos %lld is negative", (long long)start);
+    if (start != cur)
+      return fail(QL_ERR_INVALID,
+                  "positions[0] = %lld must continue from current_len (expected %lld); "
+                  "skipping, backward, or double writes are not allowed",
+                  (long long)start, (long long)cur);
+    if (start + 1 > kv->cfg.max_seq_len)
+      return fail(QL_ERR_INVALID, "positions[0] = %lld exceeds cache capacity %d",
+                  (long long)start, kv->cfg.max_seq_len);
+    seqs[b] = s;
+    ends[b] = start + 1;
+    const int tl = static_cast<int>((ends[b] + ql::kTile - 1) / ql::kTile);
+    max_tiles = std::max(max_tiles, tl);
+    total_tiles += static_cast<long long>(tl) * hkv;
+  }
+  QL_CUDA(cudaSetDevice(c->device), "set device");
+  char* scratch = nullptr;
+  int r = noalloc_scratch(c->device, &scratch);
+  if (r != QL_OK) return r;
+  r = reserve_pages(kv, seqs, ends);  // hands out pool pages; allocates nothing
+  if (r != QL_OK) return r;
+  // Split plan of ql_attn_forward, with fewer splits if the partials would not fit.
+  const int jobs = a->batch;
+  const long long slots = 2LL * c->num_sms;
+  int tps = max_tiles;
+  if (static_cast<long long>(jobs) * hkv < 2 * slots) {
+    tps = static_cast<int>(std::max<long long>(1, (total_tiles + 4 * slots - 1) / (4 * slots)));
+    tps = std::max(tps, (max_tiles + 63) / 64);
+  }
+  auto part_bytes = [&](int splits) {
+    return align256(static_cast<size_t>(jobs) * hkv * splits * 8 * 2 * sizeof(float)) +
+           static_cast<size_t>(jobs) * hkv * splits * 8 * hd * sizeof(float);
+  };
+  int max_splits = (max_tiles + tps - 1) / tps;
+  while (max_splits > 1 && part_bytes(max_splits) > kNoAllocBytes - kNoAllocCounterBytes) {
+    ++tps;
+    max_splits = (max_tiles + tps - 1) / tps;
+  }
+  int32_t* counters = reinterpret_cast<int32_t*>(scratch);
+  float* part_ml = reinterpret_cast<float*>(scratch + kNoAllocCounterBytes);
+  float* part_o = reinterpret_cast<float*>(
+      scratch + kNoAllocCounterBytes +
+      align256(static_cast<size_t>(jobs) * hkv * max_splits * 8 * 2 * sizeof(float)));
+  // The array keeps the previous call's contents: the counters must start at zero.
+  QL_CUDA(cudaMemsetAsync(counters, 0, static_cast<size_t>(jobs) * hkv * sizeof(int32_t),
+                          c->stream),
+          "clear the no-allocation counters");
+  ql::AttnArgs at{};
+  at.q = a->q;
+  at.k = a->k;
+  at.v = a->v;
+  at.in_dtype = a->in_dtype;
+  at.out = a->out;
+  at.out_dtype = a->out_dtype;
+  at.rope = nullptr;
+  at.rope_theta = a->rope_theta;
+  at.cache = view_of(kv, layer);
+  at.hq = hq;
+  at.group = group;
+  at.batch = a->batch;
+  at.new_len = 1;
+  at.scale = 1.0f / std::sqrt(static_cast<float>(hd));
+  at.fuse_append = 1;
+  at.tiles_per_split = tps;
+  at.max_splits = max_splits;
+  at.part_o = part_o;
+  at.part_ml = part_ml;
+  at.counters = counters;
+  at.status = c->status;
+  for (int b = 0; b < a->batch; ++b) {
+    at.seqs.seq[b] = seqs[b];
+    at.seqs.start[b] = static_cast<int32_t>(a->start_pos[b]);
+  }
+  QL_CUDA(ql::launch_splitkv_device_rope(at, &kv->kmap[layer], &kv->vmap[layer], jobs, c->stream),
+          "launch no-allocation decode");
+  for (int b = 0; b < a->batch; ++b) len_at(kv, layer, seqs[b]) = ends[b];
+  return QL_OK;
+}
+
 }  // extern "C"
+

@@ -41,10 +41,33 @@ __device__ __forceinline__ int64_t cache_row(const CacheView& c, int seq, int po
   return (static_cast<int64_t>(page) * c.hkv + h) * c.page + pos % c.page;
 }
 
+// Source of the RoPE (cos, sin) pairs of one position: the host-built table
+// row, or (DEV) f64 pow/sincos evaluated on the device for callers that have
+// no table (the no-allocation decode entry point).
+struct RopeSrc {
+  const double2* row;  // table row of the position, or nullptr for "no rotation"
+  double pos;
+  double theta;
+};
+
+template <bool DEV>
+__device__ __forceinline__ double2 rope_cs(const RopeSrc& r, int p, int hd) {
+  if constexpr (DEV) {
+    const double f = pow(r.theta, -2.0 * static_cast<double>(p) / static_cast<double>(hd));
+    double sn, cs;
+    sincos(r.pos * f, &sn, &cs);
+    return make_double2(cs, sn);
+  } else {
+    return r.row[p];
+  }
+}
+
 // One warp writes one cache row (one position of one KV head): K rotated
-// when rope_row is given, V as is, both converted to the cache type.
-__device__ void append_row(const void* kin, const void* vin, int in_dt, size_t in_off,
-                           const double2* rope_row, const CacheView& c, int64_t dst, int lane) {
+// when a rotation source is given, V as is, both converted to the cache type.
+template <bool DEV>
+__device__ void append_row_t(const void* kin, const void* vin, int in_dt, size_t in_off,
+                             const RopeSrc& rope, bool rotate, const CacheView& c, int64_t dst,
+                             int lane) {
   const int hd = c.hd;
   const int pairs = hd / 2;
   for (int base = 0; base < pairs; base += 32) {
@@ -56,7 +79,7 @@ __device__ void append_row(const void* kin, const void* vin, int in_dt, size_t i
       k1 = load_elem(kin, in_off + 2 * p + 1, in_dt);
       v0 = load_elem(vin, in_off + 2 * p, in_dt);
       v1 = load_elem(vin, in_off + 2 * p + 1, in_dt);
-      if (rope_row) rope_pair(k0, k1, rope_row[p], k0, k1);
+      if (rotate) rope_pair(k0, k1, rope_cs<DEV>(rope, p, hd), k0, k1);
     }
     const size_t e = static_cast<size_t>(dst) * hd + 2 * p;
     if (c.dtype == kQ8_0) {
@@ -80,6 +103,13 @@ __device__ void append_row(const void* kin, const void* vin, int in_dt, size_t i
       store_elem(c.v, e + 1, c.dtype, v1);
     }
   }
+}
+
+__device__ __forceinline__ void append_row(const void* kin, const void* vin, int in_dt,
+                                           size_t in_off, const double2* rope_row,
+                                           const CacheView& c, int64_t dst, int lane) {
+  append_row_t<false>(kin, vin, in_dt, in_off, RopeSrc{rope_row, 0.0, 0.0}, rope_row != nullptr,
+                      c, dst, lane);
 }
 
 __device__ __forceinline__ float cache_value(const CacheView& c, const void* base,
@@ -283,7 +313,7 @@ __device__ __forceinline__ void bar_consumers() {
 
 }  // namespace
 
-template <int HD, int DT>
+template <int HD, int DT, bool DEVROPE>
 __global__ void __launch_bounds__(160, 2)
     splitkv_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, int job0) {
@@ -328,7 +358,8 @@ __global__ void __launch_bounds__(160, 2)
     tma_prefetch_desc(&vmap);
   }
 
-  const double2* rope_row = a.rope + static_cast<size_t>(qpos) * (HD / 2);
+  const RopeSrc rsrc{DEVROPE ? nullptr : a.rope + static_cast<size_t>(qpos) * (HD / 2),
+                     static_cast<double>(qpos), static_cast<double>(a.rope_theta)};
   if (warp < 4) {
     // Rotated query rows of this KV head's group, split hi/lo: row g holds the
     // high part of head g, row g+8 the remainder.
@@ -338,7 +369,7 @@ __global__ void __launch_bounds__(160, 2)
       if (hg < a.group) {
         const size_t off = (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + 2 * p;
         rope_pair(load_elem(a.q, off, a.in_dtype), load_elem(a.q, off + 1, a.in_dtype),
-                  rope_row[p], y0, y1);
+                  rope_cs<DEVROPE>(rsrc, p, HD), y0, y1);
       }
       float h0, l0, h1, l1;
       split16<BF>(y0, h0, l0);
@@ -356,8 +387,8 @@ __global__ void __launch_bounds__(160, 2)
       bool ok;
       const int64_t dst = cache_row(a.cache, seq, qpos, kvh, a.status, ok);
       if (ok)
-        append_row(a.k, a.v, a.in_dtype, (static_cast<size_t>(job) * hkv + kvh) * HD, rope_row,
-                   a.cache, dst, lane);
+        append_row_t<DEVROPE>(a.k, a.v, a.in_dtype, (static_cast<size_t>(job) * hkv + kvh) * HD,
+                              rsrc, true, a.cache, dst, lane);
       fence_proxy_async_global();
     }
   }
@@ -663,13 +694,13 @@ bool splitkv_supported(int hd, int dtype, int group, int page) {
   return (dtype == kF16 || dtype == kBF16) && (hd == 64 || hd == 128);
 }
 
-template <int HD, int DT>
+template <int HD, int DT, bool DEVROPE>
 static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
                                     const CUtensorMap* vmap, int jobs, cudaStream_t s) {
   using C = SplitCfg<HD, DT>;
   static bool configured = false;
   if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(splitkv_kernel<HD, DT>,
+    cudaError_t e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(C::kSmem));
     if (e != cudaSuccess) return e;
@@ -677,22 +708,33 @@ static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
   }
   for (int j0 = 0; j0 < jobs; j0 += 65535) {
     dim3 grid(a.max_splits, a.cache.hkv, min(65535, jobs - j0));
-    splitkv_kernel<HD, DT><<<grid, 160, C::kSmem, s>>>(a, *kmap, *vmap, j0);
+    splitkv_kernel<HD, DT, DEVROPE><<<grid, 160, C::kSmem, s>>>(a, *kmap, *vmap, j0);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
 }
 
+template <bool DEVROPE>
+static cudaError_t dispatch_splitkv(const AttnArgs& a, const CUtensorMap* kmap,
+                                    const CUtensorMap* vmap, int jobs, cudaStream_t s) {
+  const int hd = a.cache.hd, dt = a.cache.dtype;
+  if (dt == kQ8_0) return launch_splitkv_t<128, kQ8_0, DEVROPE>(a, kmap, vmap, jobs, s);
+  if (hd == 128)
+    return dt == kBF16 ? launch_splitkv_t<128, kBF16, DEVROPE>(a, kmap, vmap, jobs, s)
+                       : launch_splitkv_t<128, kF16, DEVROPE>(a, kmap, vmap, jobs, s);
+  return dt == kBF16 ? launch_splitkv_t<64, kBF16, DEVROPE>(a, kmap, vmap, jobs, s)
+                     : launch_splitkv_t<64, kF16, DEVROPE>(a, kmap, vmap, jobs, s);
+}
+
 cudaError_t launch_splitkv(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,
                            int jobs, cudaStream_t s) {
-  const int hd = a.cache.hd, dt = a.cache.dtype;
-  if (dt == kQ8_0) return launch_splitkv_t<128, kQ8_0>(a, kmap, vmap, jobs, s);
-  if (hd == 128)
-    return dt == kBF16 ? launch_splitkv_t<128, kBF16>(a, kmap, vmap, jobs, s)
-                       : launch_splitkv_t<128, kF16>(a, kmap, vmap, jobs, s);
-  return dt == kBF16 ? launch_splitkv_t<64, kBF16>(a, kmap, vmap, jobs, s)
-                     : launch_splitkv_t<64, kF16>(a, kmap, vmap, jobs, s);
+  return dispatch_splitkv<false>(a, kmap, vmap, jobs, s);
+}
+
+cudaError_t launch_splitkv_device_rope(const AttnArgs& a, const CUtensorMap* kmap,
+                                       const CUtensorMap* vmap, int jobs, cudaStream_t s) {
+  return dispatch_splitkv<true>(a, kmap, vmap, jobs, s);
 }
 
 }  // namespace ql

@@ -55,6 +55,7 @@ struct AttnArgs {
   void* out;  // [batch, new_len, hq*hd]
   int32_t out_dtype;
   const double2* rope;
+  float rope_theta;  // used instead of `rope` by the device-RoPE variant
   CacheView cache;
   int32_t hq;
   int32_t group;  // hq / hkv
@@ -91,6 +92,10 @@ bool splitkv_supported(int hd, int dtype, int group, int page);
 cudaError_t launch_append(const AppendArgs& a, cudaStream_t s);
 cudaError_t launch_splitkv(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,
                            int grid_jobs, cudaStream_t s);
+// Same kernel, with the RoPE angles computed on the device (f64 pow/sincos)
+// instead of read from the host-built table; needs fuse_append and new_len 1.
+cudaError_t launch_splitkv_device_rope(const AttnArgs& a, const CUtensorMap* kmap,
+                                       const CUtensorMap* vmap, int jobs, cudaStream_t s);
 cudaError_t launch_generic(const AttnArgs& a, cudaStream_t s);
 cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s);
 
