@@ -699,12 +699,19 @@ int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   }
   int tps = max_tiles, max_splits = 1;
   if (fast) {
+    // Split the KV length when there are too few (token, KV head) jobs to
+    // cover the GPU twice, keeping at least kMinSplitTiles tiles per split
+    // (a split of one or two tiles costs more to merge than it saves) and at
+    // most 64 splits; then even the splits out.
+    constexpr int kMinSplitTiles = 4;
     const long long slots = 2LL * c->num_sms;
     if (static_cast<long long>(jobs) * hkv < 2 * slots) {
-      tps = static_cast<int>(std::max<long long>(1, (total_tiles + 4 * slots - 1) / (4 * slots)));
+      tps = static_cast<int>(std::max<long long>(1, (total_tiles + 2 * slots - 1) / (2 * slots)));
+      tps = std::max(tps, kMinSplitTiles);
       tps = std::max(tps, (max_tiles + 63) / 64);
     }
     max_splits = (max_tiles + tps - 1) / tps;
+    tps = (max_tiles + max_splits - 1) / max_splits;
   }
   // workspace: [staged q][k][v][out][part_o][part_ml][generic scratch f32][f64]
   size_t off = 0;

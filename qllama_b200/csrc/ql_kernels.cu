@@ -289,8 +289,9 @@ struct SplitCfg {
   static constexpr int kQLd = HD + 8;  // q tile row stride (elements), padded
   static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes +
                                   16 * kQLd * 2 + 64 * sizeof(float) + 16 +
-                                  2 * kStages * sizeof(uint64_t);
+                                  (2 * kStages + 1) * sizeof(uint64_t);
   static_assert(4 * 8 * HD * 4 <= kStages * kStageBytes, "merge buffer must fit the stages");
+  static_assert((2 * 64 * 8 + 8) * 4 <= kStages * kStageBytes, "split tables must fit the stages");
 };
 
 // Logical MMA k index of physical head-dim element d for int8 K rows: a
@@ -348,53 +349,32 @@ __global__ void __launch_bounds__(160, 2)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
 
+  uint64_t* appended = empty + C::kStages;  // the fused append is written and fenced
+  const bool appends = a.fuse_append && split == nsplit - 1;
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 4);
     }
+    mbar_init(appended, 1);
     fence_mbar_init();
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
   }
+  __syncthreads();
+  // Programmatic dependent launch: everything above overlaps the previous
+  // kernel; Q/K/V and the cache may come from it, so they are read only after
+  // this wait.  The next kernel may start its own set-up from here on.
+  griddep_wait();
+  griddep_launch_dependents();
 
   const RopeSrc rsrc{DEVROPE ? nullptr : a.rope + static_cast<size_t>(qpos) * (HD / 2),
                      static_cast<double>(qpos), static_cast<double>(a.rope_theta)};
-  if (warp < 4) {
-    // Rotated query rows of this KV head's group, split hi/lo: row g holds the
-    // high part of head g, row g+8 the remainder.
-    for (int idx = threadIdx.x; idx < 8 * (HD / 2); idx += 128) {
-      const int hg = idx / (HD / 2), p = idx % (HD / 2);
-      float y0 = 0.f, y1 = 0.f;
-      if (hg < a.group) {
-        const size_t off = (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + 2 * p;
-        rope_pair(load_elem(a.q, off, a.in_dtype), load_elem(a.q, off + 1, a.in_dtype),
-                  rope_cs<DEVROPE>(rsrc, p, HD), y0, y1);
-      }
-      float h0, l0, h1, l1;
-      split16<BF>(y0, h0, l0);
-      split16<BF>(y1, h1, l1);
-      const int k0 = Q8 ? q8_logical_k(2 * p) : 2 * p;
-      const int k1 = Q8 ? q8_logical_k(2 * p + 1) : 2 * p + 1;
-      const uint32_t hh = pack2<BF>(h0, h1), ll = pack2<BF>(l0, l1);
-      qs[hg * C::kQLd + k0] = static_cast<uint16_t>(hh & 0xffff);
-      qs[hg * C::kQLd + k1] = static_cast<uint16_t>(hh >> 16);
-      qs[(hg + 8) * C::kQLd + k0] = static_cast<uint16_t>(ll & 0xffff);
-      qs[(hg + 8) * C::kQLd + k1] = static_cast<uint16_t>(ll >> 16);
-    }
-    // Single-token decode: the CTA holding the last tile writes the new K/V.
-    if (a.fuse_append && split == nsplit - 1 && warp == 0) {
-      bool ok;
-      const int64_t dst = cache_row(a.cache, seq, qpos, kvh, a.status, ok);
-      if (ok)
-        append_row_t<DEVROPE>(a.k, a.v, a.in_dtype, (static_cast<size_t>(job) * hkv + kvh) * HD,
-                              rsrc, true, a.cache, dst, lane);
-      fence_proxy_async_global();
-    }
-  }
-  __syncthreads();
 
   // ------------------------------------------------------------ producer --
+  // Streams this split's tiles right away, while the consumers rotate q; only
+  // the tile holding the new token waits until its K/V row has been appended.
   if (warp == 4) {
     if (lane == 0) {
       const int* bt = a.cache.block_table + static_cast<size_t>(seq) * a.cache.pages_per_seq;
@@ -402,6 +382,7 @@ __global__ void __launch_bounds__(160, 2)
         const int st = i % C::kStages;
         if (i >= C::kStages && !mbar_wait(&empty[st], ((i / C::kStages) - 1) & 1, a.status))
           break;
+        if (appends && i == my_tiles - 1 && !mbar_wait(appended, 0, a.status)) break;
         const int p0 = (tile0 + i) * kTile;
         int page = bt[p0 / a.cache.page];
         if (page < 0 || page >= a.cache.num_pages) {
@@ -430,6 +411,41 @@ __global__ void __launch_bounds__(160, 2)
     }
     return;
   }
+
+  // Single-token decode: the CTA holding the last tile writes the new K/V
+  // (rotated K) and releases the producer for that tile.
+  if (appends && warp == 0) {
+    bool ok;
+    const int64_t dst = cache_row(a.cache, seq, qpos, kvh, a.status, ok);
+    if (ok)
+      append_row_t<DEVROPE>(a.k, a.v, a.in_dtype, (static_cast<size_t>(job) * hkv + kvh) * HD,
+                            rsrc, true, a.cache, dst, lane);
+    fence_proxy_async_global();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(appended);
+  }
+  // Rotated query rows of this KV head's group, split hi/lo: row g holds the
+  // high part of head g, row g+8 the remainder.
+  for (int idx = threadIdx.x; idx < 8 * (HD / 2); idx += 128) {
+    const int hg = idx / (HD / 2), p = idx % (HD / 2);
+    float y0 = 0.f, y1 = 0.f;
+    if (hg < a.group) {
+      const size_t off = (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + 2 * p;
+      rope_pair(load_elem(a.q, off, a.in_dtype), load_elem(a.q, off + 1, a.in_dtype),
+                rope_cs<DEVROPE>(rsrc, p, HD), y0, y1);
+    }
+    float h0, l0, h1, l1;
+    split16<BF>(y0, h0, l0);
+    split16<BF>(y1, h1, l1);
+    const int k0 = Q8 ? q8_logical_k(2 * p) : 2 * p;
+    const int k1 = Q8 ? q8_logical_k(2 * p + 1) : 2 * p + 1;
+    const uint32_t hh = pack2<BF>(h0, h1), ll = pack2<BF>(l0, l1);
+    qs[hg * C::kQLd + k0] = static_cast<uint16_t>(hh & 0xffff);
+    qs[hg * C::kQLd + k1] = static_cast<uint16_t>(hh >> 16);
+    qs[(hg + 8) * C::kQLd + k0] = static_cast<uint16_t>(ll & 0xffff);
+    qs[(hg + 8) * C::kQLd + k1] = static_cast<uint16_t>(ll >> 16);
+  }
+  bar_consumers();
 
   // ----------------------------------------------------------- consumers --
   uint32_t qa[NKS][4];
@@ -663,21 +679,37 @@ __global__ void __launch_bounds__(160, 2)
   bar_consumers();
   if (!flag[0]) return;
   __threadfence();
-  for (int idx = tid; idx < a.group * HD; idx += 128) {
-    const int hg = idx / HD, d = idx % HD;
+  // Stage every split's (m, l) once, turn them into per-split weights, then
+  // let each thread sum its outputs over the splits with independent loads.
+  float* wsm = reinterpret_cast<float*>(stages);  // [split][8] weights
+  float* msm = wsm + 64 * 8;                      // [split][8] maxima
+  float* dsm = msm + 64 * 8;                      // [8] 1 / sum of weights
+  for (int i = tid; i < nsplit * 8; i += 128) {
+    msm[i] = __ldcg(&a.part_ml[((pslot + (i >> 3)) * 8 + (i & 7)) * 2]);
+    wsm[i] = __ldcg(&a.part_ml[((pslot + (i >> 3)) * 8 + (i & 7)) * 2 + 1]);
+  }
+  bar_consumers();
+  if (tid < 8) {
     float Mx = -CUDART_INF_F;
-    for (int s = 0; s < nsplit; ++s)
-      Mx = fmaxf(Mx, __ldcg(&a.part_ml[((pslot + s) * 8 + hg) * 2]));
+    for (int s = 0; s < nsplit; ++s) Mx = fmaxf(Mx, msm[s * 8 + tid]);
     const float Mxb = Mx == -CUDART_INF_F ? 0.f : Mx;
-    float num = 0.f, den = 0.f;
+    float den = 0.f;
     for (int s = 0; s < nsplit; ++s) {
-      const float w = __ldcg(&a.part_ml[((pslot + s) * 8 + hg) * 2 + 1]) *
-                      exp2f(__ldcg(&a.part_ml[((pslot + s) * 8 + hg) * 2]) - Mxb);
-      num += w * __ldcg(&a.part_o[((pslot + s) * 8 + hg) * HD + d]);
+      const float w = wsm[s * 8 + tid] * exp2f(msm[s * 8 + tid] - Mxb);
+      wsm[s * 8 + tid] = w;
       den += w;
     }
+    dsm[tid] = 1.f / den;
+  }
+  bar_consumers();
+  for (int idx = tid; idx < a.group * HD; idx += 128) {
+    const int hg = idx / HD, d = idx % HD;
+    const float* po = a.part_o + (pslot * 8 + hg) * HD + d;
+    float num = 0.f;
+#pragma unroll 8
+    for (int s = 0; s < nsplit; ++s) num += wsm[s * 8 + hg] * __ldcg(po + static_cast<size_t>(s) * 8 * HD);
     store_elem(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d,
-               a.out_dtype, num / den);
+               a.out_dtype, num * dsm[hg]);
   }
   if (tid == 0) a.counters[static_cast<size_t>(job) * hkv + kvh] = 0;
 }
@@ -696,7 +728,7 @@ bool splitkv_supported(int hd, int dtype, int group, int page) {
 
 template <int HD, int DT, bool DEVROPE>
 static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
-                                    const CUtensorMap* vmap, int jobs, cudaStream_t s) {
+                                    const CUtensorMap* vmap, int jobs, cudaStream_t s, bool pdl) {
   using C = SplitCfg<HD, DT>;
   static bool configured = false;
   if (!configured) {
@@ -707,9 +739,17 @@ static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
     configured = true;
   }
   for (int j0 = 0; j0 < jobs; j0 += 65535) {
-    dim3 grid(a.max_splits, a.cache.hkv, min(65535, jobs - j0));
-    splitkv_kernel<HD, DT, DEVROPE><<<grid, 160, C::kSmem, s>>>(a, *kmap, *vmap, j0);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.max_splits, a.cache.hkv, min(65535, jobs - j0));
+    cfg.blockDim = dim3(160);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE>, a, *kmap, *vmap, j0);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -717,24 +757,24 @@ static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
 
 template <bool DEVROPE>
 static cudaError_t dispatch_splitkv(const AttnArgs& a, const CUtensorMap* kmap,
-                                    const CUtensorMap* vmap, int jobs, cudaStream_t s) {
+                                    const CUtensorMap* vmap, int jobs, cudaStream_t s, bool pdl) {
   const int hd = a.cache.hd, dt = a.cache.dtype;
-  if (dt == kQ8_0) return launch_splitkv_t<128, kQ8_0, DEVROPE>(a, kmap, vmap, jobs, s);
+  if (dt == kQ8_0) return launch_splitkv_t<128, kQ8_0, DEVROPE>(a, kmap, vmap, jobs, s, pdl);
   if (hd == 128)
-    return dt == kBF16 ? launch_splitkv_t<128, kBF16, DEVROPE>(a, kmap, vmap, jobs, s)
-                       : launch_splitkv_t<128, kF16, DEVROPE>(a, kmap, vmap, jobs, s);
-  return dt == kBF16 ? launch_splitkv_t<64, kBF16, DEVROPE>(a, kmap, vmap, jobs, s)
-                     : launch_splitkv_t<64, kF16, DEVROPE>(a, kmap, vmap, jobs, s);
+    return dt == kBF16 ? launch_splitkv_t<128, kBF16, DEVROPE>(a, kmap, vmap, jobs, s, pdl)
+                       : launch_splitkv_t<128, kF16, DEVROPE>(a, kmap, vmap, jobs, s, pdl);
+  return dt == kBF16 ? launch_splitkv_t<64, kBF16, DEVROPE>(a, kmap, vmap, jobs, s, pdl)
+                     : launch_splitkv_t<64, kF16, DEVROPE>(a, kmap, vmap, jobs, s, pdl);
 }
 
 cudaError_t launch_splitkv(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,
                            int jobs, cudaStream_t s) {
-  return dispatch_splitkv<false>(a, kmap, vmap, jobs, s);
+  return dispatch_splitkv<false>(a, kmap, vmap, jobs, s, true);
 }
 
 cudaError_t launch_splitkv_device_rope(const AttnArgs& a, const CUtensorMap* kmap,
                                        const CUtensorMap* vmap, int jobs, cudaStream_t s) {
-  return dispatch_splitkv<true>(a, kmap, vmap, jobs, s);
+  return dispatch_splitkv<true>(a, kmap, vmap, jobs, s, false);
 }
 
 }  // namespace ql
