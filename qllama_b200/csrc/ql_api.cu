@@ -173,6 +173,22 @@ int encode_map(CUtensorMap* m, void* base, int dtype, int hd, uint64_t rows) {
   return QL_OK;
 }
 
+// Tensor map over the rotated-q scratch [rows][hd] f16, boxes of 64 columns x
+// 128 rows with the 128-byte swizzle the tcgen05 descriptors expect.
+int encode_q_map(CUtensorMap* m, void* base, int hd, uint64_t rows) {
+  EncodeTiledFn fn = encode_tiled();
+  if (!fn) return fail(QL_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(hd), rows};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(hd) * 2};
+  cuuint32_t box[2] = {64u, 128u};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(QL_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return QL_OK;
+}
+
 // Builds (once per theta) the f64 (cos, sin) table of every position with the
 // reference formula: freq_i = theta^(-2i/hd) via pow, angle = pos * freq_i
 // (src/tensor/ops.rs:193-207), evaluated by the host libm as the reference does.
@@ -686,6 +702,8 @@ int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   const size_t ib = elem_bytes(a->in_dtype), obb = elem_bytes(a->out_dtype);
   const bool fast = kv->have_maps && ql::splitkv_supported(hd, kv->cfg.dtype, group,
                                                           kv->cfg.page_size);
+  const bool tc_prefill = kv->have_maps && n > 1 &&
+                          ql::prefill_tc_supported(hd, kv->cfg.dtype, n);
   // split planning for the tensor-core kernel
   int max_tiles = 0;
   long long total_tiles = 0;
@@ -725,6 +743,9 @@ int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   const size_t o_pm = off;
   if (fast && max_splits > 1)
     off += align256(static_cast<size_t>(jobs) * hkv * max_splits * 8 * 2 * sizeof(float));
+  const size_t q_rows = ql::prefill_q_rows(n);
+  const size_t o_qr = off;
+  if (tc_prefill) off += align256(static_cast<size_t>(a->batch) * hq * q_rows * hd * 2);
   const int gjobs = std::min(jobs, 65535);
   const size_t o_gs = off;
   if (!fast) off += align256(static_cast<size_t>(gjobs) * hq * max_len * sizeof(float));
@@ -767,6 +788,36 @@ int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
     ap.status = c->status;
     ap.seqs = st;
     QL_CUDA(ql::launch_append(ap, c->stream), "launch append");
+  }
+  if (tc_prefill) {
+    ql::PrefillArgs pa{};
+    pa.q = q;
+    pa.in_dtype = a->in_dtype;
+    pa.q_rot = reinterpret_cast<__half*>(w + o_qr);
+    pa.q_rows = static_cast<int32_t>(q_rows);
+    pa.out = out;
+    pa.out_dtype = a->out_dtype;
+    pa.rope = kv->d_rope;
+    pa.cache = cv;
+    pa.hq = hq;
+    pa.group = group;
+    pa.batch = a->batch;
+    pa.new_len = n;
+    pa.scale = 1.0f / std::sqrt(static_cast<float>(hd));  // layers.rs:432
+    pa.status = c->status;
+    pa.seqs = st;
+    CUtensorMap qmap;
+    r = encode_q_map(&qmap, w + o_qr, hd, static_cast<uint64_t>(a->batch) * hq * q_rows);
+    if (r != QL_OK) return r;
+    QL_CUDA(ql::launch_prefill_tc(pa, &qmap, &kv->kmap[layer], &kv->vmap[layer], c->stream),
+            "launch tcgen05 prefill");
+    if (a->mem == QL_MEM_HOST) {
+      QL_CUDA(cudaMemcpyAsync(a->out, out, qn * obb, cudaMemcpyDeviceToHost, c->stream),
+              "copy out");
+      QL_CUDA(cudaStreamSynchronize(c->stream), "synchronize forward");
+    }
+    for (int b = 0; b < a->batch; ++b) len_at(kv, layer, seqs[b]) = ends[b];
+    return QL_OK;
   }
   ql::AttnArgs at{};
   at.q = q;

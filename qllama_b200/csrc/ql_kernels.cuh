@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -75,6 +76,25 @@ struct AttnArgs {
   SeqTable seqs;
 };
 
+// Multi-token causal attention on the tcgen05 tensor cores (f16 cache, hd 128).
+struct PrefillArgs {
+  const void* q;       // [batch, new_len, hq, hd] pre-RoPE
+  int32_t in_dtype;
+  __half* q_rot;       // scratch [batch][hq][q_rows][hd] f16, rotated q
+  int32_t q_rows;      // new_len rounded up to the 128-row tile
+  void* out;           // [batch, new_len, hq*hd]
+  int32_t out_dtype;
+  const double2* rope;
+  CacheView cache;
+  int32_t hq;
+  int32_t group;
+  int32_t batch;
+  int32_t new_len;
+  float scale;
+  uint32_t* status;
+  SeqTable seqs;
+};
+
 struct GatherArgs {
   const int32_t* positions;  // device [n]
   int32_t n;
@@ -98,5 +118,12 @@ cudaError_t launch_splitkv_device_rope(const AttnArgs& a, const CUtensorMap* kma
                                        const CUtensorMap* vmap, int jobs, cudaStream_t s);
 cudaError_t launch_generic(const AttnArgs& a, cudaStream_t s);
 cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s);
+
+// tcgen05 prefill: when it applies, rows of the rotated-q scratch it needs,
+// and the launch (rotated-q kernel, then the attention kernel).
+bool prefill_tc_supported(int hd, int dtype, int new_len);
+size_t prefill_q_rows(int new_len);
+cudaError_t launch_prefill_tc(const PrefillArgs& a, const CUtensorMap* qmap,
+                              const CUtensorMap* kmap, const CUtensorMap* vmap, cudaStream_t s);
 
 }  // namespace ql

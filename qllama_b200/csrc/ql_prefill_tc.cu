@@ -1,0 +1,464 @@
+// ql_prefill_tc.cu -- causal GQA flash-attention prefill on the 5th-gen tensor
+// cores (tcgen05 + TMEM) for B200 (sm_100a).
+//
+// Replaces, for multi-token calls, the reference's per-head loop over the new
+// rows (src/transformer/layers.rs:430-445: q_h.k_h^T, scale, offset causal
+// mask :509-531, softmax ops.rs:292-319, probabilities.v_h).
+//
+// One CTA = 128 query rows of one query head of one sequence.  Warp roles:
+//   warp 0      TMA producer: the rotated Q tile once, then K/V tiles of 128
+//               keys (two 64-position page boxes x two 64-column halves each)
+//               into a two-stage ring; boxes of unallocated pages are read out
+//               of range, which TMA fills with zeros.
+//   warp 1      owns TMEM (512 columns) and issues every tcgen05.mma from one
+//               thread: S_j = Q K_j^T into one of two S buffers, then
+//               O += P_j V_j into the O accumulator; completion is signalled
+//               with tcgen05.commit on mbarriers.
+//   warps 4..7  softmax, one thread per query row (= TMEM lane): load S_j,
+//               scale, mask, exp2, write P_j (f16) to 128B-swizzled shared
+//               memory; keep a running max that only moves when it grows by
+//               more than 2^8, rescaling that row of O in TMEM then; finally
+//               normalise O and store the output row.
+// Operands are f16 (cache f16, q rotated in f32 then rounded to f16); the
+// accumulators are f32 in TMEM.  No cluster multicast is used anywhere.
+#include <math_constants.h>
+
+#include "ql_device.cuh"
+#include "ql_kernels.cuh"
+
+namespace ql {
+
+namespace {
+
+constexpr int kBM = 128;  // query rows per CTA
+constexpr int kBN = 128;  // keys per KV tile
+constexpr float kLog2eP = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.f;  // rescale O only when the max grows by more than 2^8
+
+// ------------------------------------------------------------ tcgen05 PTX --
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem], kind::f16, f32 accumulate.
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+      : "memory");
+}
+// 32 consecutive columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, 128-byte swizzle (layout code 2), sm100
+// descriptor version 1.  lbo/sbo in bytes.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((saddr >> 4) & 0x3FFF) |
+         (static_cast<uint64_t>((lbo >> 4) & 0x3FFF) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor, kind::f16 with f16 A/B and f32 D.
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n, bool b_mn_major) {
+  return (1u << 4) | (b_mn_major ? (1u << 16) : 0u) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+template <int HD>
+struct PrefillCfg {
+  static constexpr int kHalves = HD / 64;
+  static constexpr int kQBytes = kBM * HD * 2;          // [half][128 rows][128 B]
+  static constexpr int kKBytes = kBN * HD * 2;          // [half][128 keys][128 B]
+  static constexpr int kStageBytes = 2 * kKBytes;       // K then V
+  static constexpr int kStages = 2;
+  static constexpr int kPBytes = kBM * kBN * 2;         // [key half][128 rows][128 B]
+  static constexpr int kQOff = 0;
+  static constexpr int kStageOff = kQOff + kQBytes;
+  static constexpr int kPOff = kStageOff + kStages * kStageBytes;
+  static constexpr int kBarOff = kPOff + kPBytes;
+  static constexpr size_t kSmem = 1024 + kBarOff + 256;
+  static constexpr uint32_t kTmemCols = 512;  // S0 [0,128), S1 [128,256), O [256, 256+HD)
+  static constexpr uint32_t kOCol = 256;
+};
+
+}  // namespace
+
+template <int HD>
+__global__ void __launch_bounds__(256, 1)
+    prefill_tc_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ CUtensorMap qmap,
+                      const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap) {
+  using C = PrefillCfg<HD>;
+  const int n_qt = (a.new_len + kBM - 1) / kBM;
+  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // heaviest tiles first
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / a.group;
+  const int seq = a.seqs.seq[b];
+  const int start = a.seqs.start[b];
+  const int q_first = qt * kBM;
+  const int q_last = min(a.new_len, q_first + kBM) - 1;  // last valid row of the tile
+  const int kv_end = start + q_last + 1;                 // keys visible to the last row
+  const int n_kv = (kv_end + kBN - 1) / kBN;
+  const int hkv = a.cache.hkv;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* qsm = smem + C::kQOff;
+  uint8_t* stg = smem + C::kStageOff;
+  uint8_t* psm = smem + C::kPOff;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
+  uint64_t* q_full = bars + 0;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* s_empty = bars + 7;   // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* pv_done = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&qmap);
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  griddep_wait();
+
+  if (warp == 0) {
+    // -------------------------------------------------------- producer --
+    if (lane == 0) {
+      const int qrow = (b * a.hq + h) * a.q_rows + q_first;
+      mbar_arrive_expect_tx(q_full, C::kQBytes);
+#pragma unroll
+      for (int hf = 0; hf < C::kHalves; ++hf)
+        tma_load_2d(qsm + hf * (kBM * 128), &qmap, hf * 64, qrow, q_full);
+      const int* bt = a.cache.block_table + static_cast<size_t>(seq) * a.cache.pages_per_seq;
+      const int oob_row = a.cache.num_pages * hkv * a.cache.page;  // past the pool: zero fill
+      for (int j = 0; j < n_kv; ++j) {
+        const int st = j & 1;
+        if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, a.status)) break;
+        uint8_t* ks = stg + st * C::kStageBytes;
+        uint8_t* vs = ks + C::kKBytes;
+        mbar_arrive_expect_tx(&kv_full[st], C::kStageBytes);
+#pragma unroll
+        for (int sub = 0; sub < 2; ++sub) {
+          const int key0 = j * kBN + sub * 64;
+          const int lp = key0 / a.cache.page;
+          int row = oob_row;
+          if (lp < a.cache.pages_per_seq) {
+            const int page = bt[lp];
+            if (page >= 0 && page < a.cache.num_pages)
+              row = (page * hkv + kvh) * a.cache.page + key0 % a.cache.page;
+          }
+#pragma unroll
+          for (int hf = 0; hf < C::kHalves; ++hf) {
+            tma_load_2d(ks + hf * (kBN * 128) + sub * 8192, &kmap, hf * 64, row, &kv_full[st]);
+            tma_load_2d(vs + hf * (kBN * 128) + sub * 8192, &vmap, hf * 64, row, &kv_full[st]);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA --
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = instr_desc(kBM, kBN, false);
+      constexpr uint32_t idesc_o = instr_desc(kBM, HD, true);
+      const uint32_t qaddr = smem_u32(qsm), paddr = smem_u32(psm);
+      bool ok = mbar_wait(q_full, 0, a.status);
+      auto issue_s = [&](int j) {
+        const uint32_t kaddr = smem_u32(stg + (j & 1) * C::kStageBytes);
+        const uint32_t d = tmem + (j & 1) * kBN;
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          const uint32_t off = (ks >> 2) * (kBN * 128) + (ks & 3) * 32;
+          const uint32_t qoff = (ks >> 2) * (kBM * 128) + (ks & 3) * 32;
+          tc_mma(d, smem_desc(qaddr + qoff, 16, 1024), smem_desc(kaddr + off, 16, 1024), idesc_s,
+                 ks > 0);
+        }
+        tc_commit(&s_full[j & 1]);
+      };
+      if (ok) ok = mbar_wait(&kv_full[0], 0, a.status);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (j + 1 < n_kv) {
+          ok = mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, a.status);
+          if (ok && j + 1 >= 2)
+            ok = mbar_wait(&s_empty[(j + 1) & 1], (((j + 1) >> 1) - 1) & 1, a.status);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
+        if (!mbar_wait(p_full, j & 1, a.status)) break;
+        tc_fence_after();
+        const uint32_t vaddr = smem_u32(stg + (j & 1) * C::kStageBytes + C::kKBytes);
+#pragma unroll
+        for (int ks = 0; ks < kBN / 16; ++ks) {
+          const uint32_t poff = (ks >> 2) * (kBM * 128) + (ks & 3) * 32;
+          tc_mma(tmem + C::kOCol, smem_desc(paddr + poff, 16, 1024),
+                 smem_desc(vaddr + ks * 2048, kBN * 128, 1024), idesc_o, (j > 0 || ks > 0));
+        }
+        tc_commit(pv_done);
+        tc_commit(&kv_empty[j & 1]);
+      }
+    }
+  } else if (warp >= 4) {
+    // --------------------------------------------------------- softmax --
+    const int r = threadIdx.x - 128;  // query row in the tile == TMEM lane
+    const int row = q_first + r;
+    const int qpos = start + row;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const float sl2 = a.scale * kLog2eP;
+    float m_used = -CUDART_INF_F, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, a.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float x[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c) {
+        float v[32];
+        tmem_ld32(lane_addr + (j & 1) * kBN + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[c * 32 + i] = v[i];
+      }
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&s_empty[j & 1]);
+      const int key0 = j * kBN;
+      const bool masked = key0 + kBN - 1 > qpos;
+      float mx = -CUDART_INF_F;
+#pragma unroll
+      for (int i = 0; i < kBN; ++i) {
+        float v = x[i] * sl2;
+        if (masked && key0 + i > qpos) v = -CUDART_INF_F;
+        x[i] = v;
+        mx = fmaxf(mx, v);
+      }
+      float corr = 1.f;
+      bool rescale = false;
+      if (mx > m_used + kRescaleLog2 || m_used == -CUDART_INF_F) {
+        const float m_new = mx == -CUDART_INF_F ? 0.f : mx;
+        corr = exp2f(m_used - m_new);  // 0 while nothing has been accumulated
+        rescale = j > 0 && m_used != -CUDART_INF_F;
+        m_used = m_new;
+      }
+      float psum = 0.f;
+#pragma unroll
+      for (int i = 0; i < kBN; ++i) {
+        x[i] = exp2f(x[i] - m_used);  // p, in place
+        psum += x[i];
+      }
+      l = l * corr + psum;
+      if (j > 0 && !mbar_wait(pv_done, (j - 1) & 1, a.status)) {
+        ok = false;
+        break;
+      }
+      if (rescale) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < HD / 32; ++c) {
+          float v[32];
+          tmem_ld32(lane_addr + C::kOCol + c * 32, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= corr;
+          tmem_st32(lane_addr + C::kOCol + c * 32, v);
+        }
+        tmem_wait_st();
+      }
+      // P row (f16): 16 chunks of 8 keys, chunk c of key half c/8 at its swizzled slot.
+#pragma unroll
+      for (int c = 0; c < kBN / 8; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          __half2 hp = __floats2half2_rn(x[8 * c + 2 * e], x[8 * c + 2 * e + 1]);
+          w[e] = *reinterpret_cast<uint32_t*>(&hp);
+        }
+        const uint32_t off = (c >> 3) * (kBM * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(psm + off) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // ---- epilogue: O / l for the valid rows
+    if (ok && mbar_wait(pv_done, (n_kv - 1) & 1, a.status)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      const size_t obase = ((static_cast<size_t>(b) * a.new_len + row) * a.hq + h) * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        float v[32];
+        tmem_ld32(lane_addr + C::kOCol + c * 32, v);
+        tmem_wait_ld();
+        if (row < a.new_len) {
+          if (a.out_dtype == kF32) {
+            float4* o4 = reinterpret_cast<float4*>(static_cast<float*>(a.out) + obase + c * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              o4[i] = make_float4(v[4 * i] * inv, v[4 * i + 1] * inv, v[4 * i + 2] * inv,
+                                  v[4 * i + 3] * inv);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) store_elem(a.out, obase + c * 32 + i, a.out_dtype, v[i] * inv);
+          }
+        }
+      }
+    }
+  }
+  griddep_launch_dependents();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------ rotated-Q scratch --
+// One warp per (sequence, token, query head): RoPE with the host table (bit
+// for bit the reference's rotation), rounded to f16, at
+// q_out[((b*hq + h)*q_rows + t)*hd + d].
+__global__ void __launch_bounds__(128) rope_q_kernel(const __grid_constant__ PrefillArgs a) {
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rows = a.batch * a.new_len * a.hq;
+  if (w >= rows) return;
+  const int h = w % a.hq, t = (w / a.hq) % a.new_len, b = w / (a.hq * a.new_len);
+  const int hd = a.cache.hd;
+  const int pos = a.seqs.start[b] + t;
+  const double2* rr = a.rope + static_cast<size_t>(pos) * (hd / 2);
+  const size_t in = (static_cast<size_t>(b * a.new_len + t) * a.hq + h) * hd;
+  __half* out = a.q_rot + ((static_cast<size_t>(b) * a.hq + h) * a.q_rows + t) * hd;
+  for (int p = lane; p < hd / 2; p += 32) {
+    float y0, y1;
+    rope_pair(load_elem(a.q, in + 2 * p, a.in_dtype), load_elem(a.q, in + 2 * p + 1, a.in_dtype),
+              rr[p], y0, y1);
+    *reinterpret_cast<__half2*>(out + 2 * p) = __floats2half2_rn(y0, y1);
+  }
+}
+
+bool prefill_tc_supported(int hd, int dtype, int new_len) {
+  return hd == 128 && dtype == kF16 && new_len >= 64;
+}
+
+size_t prefill_q_rows(int new_len) { return static_cast<size_t>((new_len + kBM - 1) / kBM) * kBM; }
+
+cudaError_t launch_prefill_tc(const PrefillArgs& a, const CUtensorMap* qmap,
+                              const CUtensorMap* kmap, const CUtensorMap* vmap, cudaStream_t s) {
+  using C = PrefillCfg<128>;
+  const int rows = a.batch * a.new_len * a.hq;
+  rope_q_kernel<<<(rows + 3) / 4, 128, 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  static bool configured = false;
+  if (!configured) {
+    e = cudaFuncSetAttribute(prefill_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(C::kSmem));
+    if (e != cudaSuccess) return e;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((a.new_len + kBM - 1) / kBM, a.hq, a.batch);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, prefill_tc_kernel<128>, a, *qmap, *kmap, *vmap);
+}
+
+}  // namespace ql

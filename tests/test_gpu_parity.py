@@ -274,3 +274,36 @@ def test_long_context_q8_0_decode_sample(ctx):
     with pytest.raises(qb.QllamaError, match="capacity"):
         qb.attention_forward(p.gpu, 0, gu.to_device(q, "bf16"), gu.to_device(k, "bf16"),
                              gu.to_device(v, "bf16"), [L, L], hq, hkv, hd, theta)
+
+
+@pytest.mark.parametrize("batch,n,start,hq,hkv", [
+    (2, 200, 0, 8, 2),      # ragged last 128-row tile, GQA 4
+    (1, 512, 100, 16, 4),   # non-zero start: offset causal mask
+    (3, 128, 37, 4, 4),     # MHA, start inside a KV tile
+    (1, 1500, 0, 8, 8),     # many KV tiles: pipeline wrap, O rescaling
+    (1, 64, 0, 8, 1),       # one half-filled tile, GQA 8
+])
+def test_tcgen05_prefill_parity(ctx, batch, n, start, hq, hkv):
+    """Multi-token calls on an f16 cache with head_dim 128 run the tcgen05/TMEM kernel."""
+    rng = np.random.default_rng(n * 7 + start)
+    hd, theta = 128, 500000.0
+    p = gu.Pair(ctx, "f16", 1, start + n + 64, hkv, hd, batch)
+    for s in range(batch):
+        if start:
+            p.prefill_rows(rng, 0, s, start, theta)
+    q = gu.rounded(gu.normal(rng, (batch, n, hq, hd)), "bf16")
+    k = gu.rounded(gu.normal(rng, (batch, n, hkv, hd)), "bf16")
+    v = gu.rounded(gu.normal(rng, (batch, n, hkv, hd)), "bf16")
+    starts = np.full(batch, start, np.int64)
+    out = qb.attention_forward(p.gpu, 0, gu.to_device(q, "bf16"), gu.to_device(k, "bf16"),
+                               gu.to_device(v, "bf16"), starts, hq, hkv, hd, theta)
+    p.gpu.ctx.synchronize()
+    ref = p.oracle_forward(0, q, k, v, starts, hq, theta)
+    assert gu.max_err(out, ref) <= TOL_16
+    # a decode step after the prefill sees the appended rows
+    q1 = gu.rounded(gu.normal(rng, (batch, 1, hq, hd)), "bf16")
+    k1 = gu.rounded(gu.normal(rng, (batch, 1, hkv, hd)), "bf16")
+    out1 = qb.attention_forward(p.gpu, 0, gu.to_device(q1, "bf16"), gu.to_device(k1, "bf16"),
+                                gu.to_device(k1, "bf16"), starts + n, hq, hkv, hd, theta)
+    ref1 = p.oracle_forward(0, q1, k1, k1, starts + n, hq, theta)
+    assert gu.max_err(out1, ref1) <= TOL_16
