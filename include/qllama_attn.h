@@ -99,6 +99,11 @@ int ql_kv_destroy(ql_kv* kv);
 int ql_kv_clear(ql_kv* kv);
 /* Clear one sequence slot and return its pages to the pool. */
 int ql_kv_clear_seq(ql_kv* kv, int32_t seq);
+/* Shorten sequence `seq` to `new_len` positions in every layer (each layer must
+ * hold at least that many); pages are kept and later writes continue from
+ * new_len.  No counterpart in the reference, whose cache only appends or
+ * clears; it serves roll-back (a rejected speculative draft, a replayed step). */
+int ql_kv_truncate(ql_kv* kv, int32_t seq, int64_t new_len);
 /* KvCache::seq_len (cache.rs:245-247): written prefix of layer 0 of `seq`. */
 int ql_kv_seq_len(const ql_kv* kv, int32_t seq, int64_t* out_len);
 /* Written prefix of one layer of one sequence. */

@@ -33,7 +33,7 @@ EXPORTS = (
     "ql_version", "ql_last_error", "ql_ctx_create", "ql_ctx_destroy", "ql_ctx_set_stream",
     "ql_ctx_synchronize", "ql_kv_create", "ql_kv_destroy", "ql_kv_clear", "ql_kv_clear_seq",
     "ql_kv_seq_len", "ql_kv_layer_len", "ql_kv_update", "ql_kv_get", "ql_attn_forward",
-    "ql_attn_decode_noalloc",
+    "ql_attn_decode_noalloc", "ql_kv_truncate",
 )
 
 
@@ -93,6 +93,7 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
     L.ql_kv_destroy.argtypes = [vp]
     L.ql_kv_clear.argtypes = [vp]
     L.ql_kv_clear_seq.argtypes = [vp, i32]
+    L.ql_kv_truncate.argtypes = [vp, i32, i64]
     L.ql_kv_seq_len.argtypes = [vp, i32, i64p]
     L.ql_kv_layer_len.argtypes = [vp, i32, i32, i64p]
     L.ql_kv_update.argtypes = [vp, vp, i32, i32, vp, i64p, i32, vp, i64p, i32, i32, i32p, i64,
@@ -158,7 +159,10 @@ class Context:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown: the library may already be gone
+            pass
 
 
 class KvCache:
@@ -210,6 +214,10 @@ class KvCache:
     def clear_seq(self, seq: int) -> None:
         _check(load().ql_kv_clear_seq(self._h, seq))
 
+    def truncate(self, seq: int, new_len: int) -> None:
+        """Roll sequence `seq` back to `new_len` positions in every layer (pages kept)."""
+        _check(load().ql_kv_truncate(self._h, seq, new_len))
+
     def seq_len(self, seq: int = 0) -> int:
         out = ctypes.c_int64()
         _check(load().ql_kv_seq_len(self._h, seq, ctypes.byref(out)))
@@ -226,7 +234,10 @@ class KvCache:
             self._h = None
 
     def __del__(self):
-        self.close()
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown: the library may already be gone
+            pass
 
 
 def attention_forward(kv: KvCache, layer: int, q, k, v, start_pos, num_heads: int,

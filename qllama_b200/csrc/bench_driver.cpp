@@ -5,7 +5,8 @@
 // per step; this loop makes the same sequence of ql_attn_forward calls from
 // native code, so the measured time is the library's, not an interpreter's.
 // `prefill` tokens are written at positions 0..prefill-1, then `steps` single
-// tokens from position `decode_start` on (either phase may be empty).
+// tokens, sequence b from position decode_starts[b] on (either phase may be
+// empty).
 // Buffers are device pointers laid out as
 //   prefill q/k/v: [layers][batch][prefill][heads][hd]
 //   decode  q/k/v: [steps][layers][batch][1][heads][hd]
@@ -18,7 +19,8 @@
 #include "../../include/qllama_attn.h"
 
 extern "C" int qlb_run_job(ql_ctx* ctx, ql_kv* kv, int32_t layers, int32_t batch,
-                           int32_t prefill, int32_t steps, int32_t decode_start, int32_t hq,
+                           int32_t prefill, int32_t steps, const int64_t* decode_starts,
+                           int32_t hq,
                            int32_t hkv, int32_t hd,
                            float theta, int32_t in_dtype, int32_t out_dtype, const void* pq,
                            const void* pk, const void* pv, void* pout, const void* dq,
@@ -54,7 +56,7 @@ extern "C" int qlb_run_job(ql_ctx* ctx, ql_kv* kv, int32_t layers, int32_t batch
       if (rc != QL_OK) return rc;
     }
   }
-  for (int b = 0; b < batch; ++b) starts[b] = decode_start;
+  for (int b = 0; b < batch; ++b) starts[b] = decode_starts[b];
   a.new_len = 1;
   const size_t qs = (size_t)batch * hq * hd, ks = (size_t)batch * hkv * hd;
   for (int s = 0; s < steps; ++s) {

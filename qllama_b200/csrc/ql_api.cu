@@ -481,6 +481,19 @@ int ql_kv_clear_seq(ql_kv* kv, int32_t seq) {
   return QL_OK;
 }
 
+int ql_kv_truncate(ql_kv* kv, int32_t seq, int64_t new_len) {
+  if (!kv) return fail(QL_ERR_INVALID, "ql_kv_truncate: kv is NULL");
+  if (seq < 0 || seq >= kv->cfg.max_batch)
+    return fail(QL_ERR_INVALID, "sequence %d out of range (cache has %d slots)", seq,
+                kv->cfg.max_batch);
+  for (int l = 0; l < kv->cfg.num_layers; ++l)
+    if (new_len < 0 || new_len > len_at(kv, l, seq))
+      return fail(QL_ERR_INVALID, "cannot truncate layer %d of sequence %d to %lld positions "
+                  "(it holds %lld)", l, seq, (long long)new_len, (long long)len_at(kv, l, seq));
+  for (int l = 0; l < kv->cfg.num_layers; ++l) len_at(kv, l, seq) = new_len;
+  return QL_OK;
+}
+
 int ql_kv_seq_len(const ql_kv* kv, int32_t seq, int64_t* out_len) {
   if (!kv || !out_len) return fail(QL_ERR_INVALID, "ql_kv_seq_len: NULL argument");
   if (seq < 0 || seq >= kv->cfg.max_batch)

@@ -307,3 +307,26 @@ def test_tcgen05_prefill_parity(ctx, batch, n, start, hq, hkv):
                                 gu.to_device(k1, "bf16"), starts + n, hq, hkv, hd, theta)
     ref1 = p.oracle_forward(0, q1, k1, k1, starts + n, hq, theta)
     assert gu.max_err(out1, ref1) <= TOL_16
+
+
+def test_truncate_rolls_back_and_rewrites(ctx):
+    """ql_kv_truncate: roll a sequence back, write new rows over the old positions."""
+    rng = np.random.default_rng(21)
+    hd, hq, hkv, theta = 64, 8, 2, 10000.0
+    p = gu.Pair(ctx, "f16", 2, 256, hkv, hd, 1)
+    for layer in (0, 1):
+        p.prefill_rows(rng, layer, 0, 100, theta)
+    with pytest.raises(qb.QllamaError, match="cannot truncate"):
+        p.gpu.truncate(0, 101)
+    p.gpu.truncate(0, 60)
+    assert p.gpu.seq_len(0) == 60 and p.gpu.layer_len(1, 0) == 60
+    # the oracle has no roll-back: rebuild its cache with the first 60 rows
+    kg, vg = p.gpu.get(0, np.arange(60))
+    fresh = oracle.KvCache(2, 256, hkv, hd, oracle.F16)
+    fresh.update(0, kg, vg, np.arange(60))
+    q, k, v = (gu.normal(rng, (1, 1, h, hd)) for h in (hq, hkv, hkv))
+    out = qb.attention_forward(p.gpu, 0, gu.to_device(q, "f32"), gu.to_device(k, "f32"),
+                               gu.to_device(v, "f32"), [60], hq, hkv, hd, theta)
+    ref = oracle.attention_with_cache(fresh, 0, q[0], k[0], v[0], 60, hq, hkv, hd, theta)
+    assert gu.max_err(out[0], ref) <= TOL_16
+    assert p.gpu.layer_len(0, 0) == 61 and p.gpu.layer_len(1, 0) == 60
