@@ -5,20 +5,25 @@
 // rows (src/transformer/layers.rs:430-445: q_h.k_h^T, scale, offset causal
 // mask :509-531, softmax ops.rs:292-319, probabilities.v_h).
 //
-// One CTA = 128 query rows of one query head of one sequence.  Warp roles:
-//   warp 0      TMA producer: the rotated Q tile once, then K/V tiles of 128
+// One CTA = 128 query rows of NQ query heads (two heads of one KV group when
+// the group size is even) of one sequence; the heads share every K/V tile.
+// Warp roles:
+//   warp 0      TMA producer: the rotated Q tiles once, then K/V tiles of 128
 //               keys (two 64-position page boxes x two 64-column halves each)
 //               into a two-stage ring; boxes of unallocated pages are read out
 //               of range, which TMA fills with zeros.
 //   warp 1      owns TMEM (512 columns) and issues every tcgen05.mma from one
-//               thread: S_j = Q K_j^T into one of two S buffers, then
-//               O += P_j V_j into the O accumulator; completion is signalled
-//               with tcgen05.commit on mbarriers.
-//   warps 4..7  softmax, one thread per query row (= TMEM lane): load S_j,
-//               scale, mask, exp2, write P_j (f16) to 128B-swizzled shared
-//               memory; keep a running max that only moves when it grows by
-//               more than 2^8, rescaling that row of O in TMEM then; finally
-//               normalise O and store the output row.
+//               thread: S_q(j) = Q_q K_j^T (A and B from shared memory) and
+//               O_q += P_q(j) V_j with P taken from TMEM; completion is
+//               signalled with tcgen05.commit on mbarriers.  The two heads'
+//               MMAs interleave, so one head's MMAs run while the other
+//               head's softmax warpgroup works.
+//   warps 4..   one softmax warpgroup per head, one thread per query row (=
+//               TMEM lane): read S (two passes of 32 columns: max, then
+//               exp2), write P as f16 pairs over S's first 64 columns; keep a
+//               running max that moves only when it grows by more than 2^8,
+//               rescaling that row of O in TMEM then; finally normalise O and
+//               store the output row.
 // Operands are f16 (cache f16, q rotated in f32 then rounded to f16); the
 // accumulators are f32 in TMEM.  No cluster multicast is used anywhere.
 #include <math_constants.h>
@@ -127,40 +132,68 @@ __host__ __device__ constexpr uint32_t instr_desc(int m, int n, bool b_mn_major)
          (static_cast<uint32_t>(m >> 4) << 24);
 }
 
-template <int HD>
+// D[tmem] (+)= A[tmem] * B[smem], kind::f16 (A K-major in TMEM, two f16 per column).
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+          d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0)
+      : "memory");
+}
+// 16 consecutive 32-bit columns of this thread's lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ float ex2_approx(float x) {  // 2^x; -inf -> +0
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// NQ query tiles (heads 2p, 2p+1 of one KV group when NQ == 2) share every
+// K/V tile.  TMEM columns: S_q at [128q, 128q+128) with P_q (f16 pairs)
+// written over its first 64 columns; O_q at [256 + 128q, 256 + 128q + HD).
+template <int HD, int NQ>
 struct PrefillCfg {
   static constexpr int kHalves = HD / 64;
-  static constexpr int kQBytes = kBM * HD * 2;          // [half][128 rows][128 B]
-  static constexpr int kKBytes = kBN * HD * 2;          // [half][128 keys][128 B]
-  static constexpr int kStageBytes = 2 * kKBytes;       // K then V
+  static constexpr int kQBytes = kBM * HD * 2;     // per query tile: [half][128 rows][128 B]
+  static constexpr int kKBytes = kBN * HD * 2;     // [half][128 keys][128 B]
+  static constexpr int kStageBytes = 2 * kKBytes;  // K then V
   static constexpr int kStages = 2;
-  static constexpr int kPBytes = kBM * kBN * 2;         // [key half][128 rows][128 B]
   static constexpr int kQOff = 0;
-  static constexpr int kStageOff = kQOff + kQBytes;
-  static constexpr int kPOff = kStageOff + kStages * kStageBytes;
-  static constexpr int kBarOff = kPOff + kPBytes;
+  static constexpr int kStageOff = kQOff + NQ * kQBytes;
+  static constexpr int kBarOff = kStageOff + kStages * kStageBytes;
   static constexpr size_t kSmem = 1024 + kBarOff + 256;
-  static constexpr uint32_t kTmemCols = 512;  // S0 [0,128), S1 [128,256), O [256, 256+HD)
+  static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kOCol = 256;
+  static constexpr int kThreads = 128 * (1 + NQ);  // warpgroup 0: TMA + MMA; one per tile
 };
 
 }  // namespace
 
-template <int HD>
-__global__ void __launch_bounds__(256, 1)
+template <int HD, int NQ>
+__global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ CUtensorMap qmap,
                       const __grid_constant__ CUtensorMap kmap,
                       const __grid_constant__ CUtensorMap vmap) {
-  using C = PrefillCfg<HD>;
+  using C = PrefillCfg<HD, NQ>;
   const int n_qt = (a.new_len + kBM - 1) / kBM;
   const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // heaviest tiles first
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int kvh = h / a.group;
+  const int h0 = blockIdx.y * NQ, b = blockIdx.z;
+  const int kvh = h0 / a.group;
   const int seq = a.seqs.seq[b];
   const int start = a.seqs.start[b];
   const int q_first = qt * kBM;
-  const int q_last = min(a.new_len, q_first + kBM) - 1;  // last valid row of the tile
-  const int kv_end = start + q_last + 1;                 // keys visible to the last row
+  const int q_last = min(a.new_len, q_first + kBM) - 1;
+  const int kv_end = start + q_last + 1;  // keys visible to the last row
   const int n_kv = (kv_end + kBN - 1) / kBN;
   const int hkv = a.cache.hkv;
 
@@ -169,16 +202,14 @@ __global__ void __launch_bounds__(256, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t* qsm = smem + C::kQOff;
   uint8_t* stg = smem + C::kStageOff;
-  uint8_t* psm = smem + C::kPOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;   // [2]
   uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
-  uint64_t* s_empty = bars + 7;   // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* pv_done = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* s_full = bars + 5;    // [NQ] S_q(j) computed (and everything issued before it)
+  uint64_t* p_full = bars + 7;    // [NQ] P_q(j) written, O_q rescaled if needed
+  uint64_t* o_done = bars + 9;    // all MMAs complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -187,11 +218,12 @@ __global__ void __launch_bounds__(256, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(pv_done, 1);
+    for (int q = 0; q < NQ; ++q) {
+      mbar_init(&s_full[q], 1);
+      mbar_init(&p_full[q], 128);
+    }
+    mbar_init(o_done, 1);
     fence_mbar_init();
     tma_prefetch_desc(&qmap);
     tma_prefetch_desc(&kmap);
@@ -210,11 +242,14 @@ __global__ void __launch_bounds__(256, 1)
   if (warp == 0) {
     // -------------------------------------------------------- producer --
     if (lane == 0) {
-      const int qrow = (b * a.hq + h) * a.q_rows + q_first;
-      mbar_arrive_expect_tx(q_full, C::kQBytes);
+      mbar_arrive_expect_tx(q_full, NQ * C::kQBytes);
 #pragma unroll
-      for (int hf = 0; hf < C::kHalves; ++hf)
-        tma_load_2d(qsm + hf * (kBM * 128), &qmap, hf * 64, qrow, q_full);
+      for (int q = 0; q < NQ; ++q) {
+        const int qrow = (b * a.hq + h0 + q) * a.q_rows + q_first;
+#pragma unroll
+        for (int hf = 0; hf < C::kHalves; ++hf)
+          tma_load_2d(qsm + q * C::kQBytes + hf * (kBM * 128), &qmap, hf * 64, qrow, q_full);
+      }
       const int* bt = a.cache.block_table + static_cast<size_t>(seq) * a.cache.pages_per_seq;
       const int oob_row = a.cache.num_pages * hkv * a.cache.page;  // past the pool: zero fill
       for (int j = 0; j < n_kv; ++j) {
@@ -243,143 +278,145 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA --
+    // Issue order per KV tile j (the tensor core executes them in order):
+    //   PV_0(j-1) S_0(j) PV_1(j-1) S_1(j) ...   so that while one softmax
+    //   warpgroup works on S_q(j), the other query tile's MMAs run.
     if (lane == 0) {
       constexpr uint32_t idesc_s = instr_desc(kBM, kBN, false);
       constexpr uint32_t idesc_o = instr_desc(kBM, HD, true);
-      const uint32_t qaddr = smem_u32(qsm), paddr = smem_u32(psm);
+      const uint32_t qaddr = smem_u32(qsm);
       bool ok = mbar_wait(q_full, 0, a.status);
-      auto issue_s = [&](int j) {
+      auto issue_s = [&](int q, int j) {
         const uint32_t kaddr = smem_u32(stg + (j & 1) * C::kStageBytes);
-        const uint32_t d = tmem + (j & 1) * kBN;
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * (kBN * 128) + (ks & 3) * 32;
-          const uint32_t qoff = (ks >> 2) * (kBM * 128) + (ks & 3) * 32;
-          tc_mma(d, smem_desc(qaddr + qoff, 16, 1024), smem_desc(kaddr + off, 16, 1024), idesc_s,
-                 ks > 0);
+          const uint32_t koff = (ks >> 2) * (kBN * 128) + (ks & 3) * 32;
+          const uint32_t qoff = q * C::kQBytes + (ks >> 2) * (kBM * 128) + (ks & 3) * 32;
+          tc_mma(tmem + q * kBN, smem_desc(qaddr + qoff, 16, 1024),
+                 smem_desc(kaddr + koff, 16, 1024), idesc_s, ks > 0);
         }
-        tc_commit(&s_full[j & 1]);
+        tc_commit(&s_full[q]);
       };
-      if (ok) ok = mbar_wait(&kv_full[0], 0, a.status);
-      if (ok) {
-        tc_fence_after();
-        issue_s(0);
-      }
-      for (int j = 0; ok && j < n_kv; ++j) {
-        if (j + 1 < n_kv) {
-          ok = mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, a.status);
-          if (ok && j + 1 >= 2)
-            ok = mbar_wait(&s_empty[(j + 1) & 1], (((j + 1) >> 1) - 1) & 1, a.status);
-          if (!ok) break;
-          tc_fence_after();
-          issue_s(j + 1);
-        }
-        if (!mbar_wait(p_full, j & 1, a.status)) break;
-        tc_fence_after();
+      auto issue_pv = [&](int q, int j) {
         const uint32_t vaddr = smem_u32(stg + (j & 1) * C::kStageBytes + C::kKBytes);
 #pragma unroll
-        for (int ks = 0; ks < kBN / 16; ++ks) {
-          const uint32_t poff = (ks >> 2) * (kBM * 128) + (ks & 3) * 32;
-          tc_mma(tmem + C::kOCol, smem_desc(paddr + poff, 16, 1024),
-                 smem_desc(vaddr + ks * 2048, kBN * 128, 1024), idesc_o, (j > 0 || ks > 0));
+        for (int ks = 0; ks < kBN / 16; ++ks)
+          tc_mma_ts(tmem + C::kOCol + q * 128, tmem + q * kBN + ks * 8,
+                    smem_desc(vaddr + ks * 2048, kBN * 128, 1024), idesc_o, (j > 0 || ks > 0));
+      };
+      for (int j = 0; ok && j < n_kv; ++j) {
+        ok = mbar_wait(&kv_full[j & 1], (j >> 1) & 1, a.status);
+        if (!ok) break;
+        for (int q = 0; q < NQ; ++q) {
+          if (j > 0) {  // P_q(j-1) is in S_q's columns: consume it before S_q(j) overwrites them
+            if (!mbar_wait(&p_full[q], (j - 1) & 1, a.status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(q, j - 1);
+            if (q == NQ - 1) tc_commit(&kv_empty[(j - 1) & 1]);
+          }
+          tc_fence_after();
+          issue_s(q, j);
         }
-        tc_commit(pv_done);
-        tc_commit(&kv_empty[j & 1]);
       }
+      for (int q = 0; ok && q < NQ; ++q) {
+        if (!mbar_wait(&p_full[q], (n_kv - 1) & 1, a.status)) break;
+        tc_fence_after();
+        issue_pv(q, n_kv - 1);
+      }
+      tc_commit(o_done);
     }
   } else if (warp >= 4) {
     // --------------------------------------------------------- softmax --
-    const int r = threadIdx.x - 128;  // query row in the tile == TMEM lane
+    const int q = (warp - 4) >> 2;     // which query tile this warpgroup serves
+    const int r = threadIdx.x & 127;   // row in the tile == TMEM lane
+    const int h = h0 + q;
     const int row = q_first + r;
     const int qpos = start + row;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t s_col = q * kBN, o_col = C::kOCol + q * 128;
     const float sl2 = a.scale * kLog2eP;
     float m_used = -CUDART_INF_F, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, a.status)) {
+      if (!mbar_wait(&s_full[q], j & 1, a.status)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float x[kBN];
+      const int key0 = j * kBN;
+      const bool masked = key0 + kBN - 1 > qpos;
+      // pass 1: row max of the scaled scores
+      float mx = -CUDART_INF_F;
 #pragma unroll
       for (int c = 0; c < kBN / 32; ++c) {
         float v[32];
-        tmem_ld32(lane_addr + (j & 1) * kBN + c * 32, v);
+        tmem_ld32(lane_addr + s_col + c * 32, v);
+        tmem_wait_ld();
+        float m4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[c * 32 + i] = v[i];
+        for (int i = 0; i < 32; ++i) {
+          const bool dead = masked && key0 + c * 32 + i > qpos;
+          m4[i & 3] = fmaxf(m4[i & 3], dead ? -CUDART_INF_F : v[i]);
+        }
+        mx = fmaxf(mx, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
       }
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&s_empty[j & 1]);
-      const int key0 = j * kBN;
-      const bool masked = key0 + kBN - 1 > qpos;
-      float mx = -CUDART_INF_F;
-#pragma unroll
-      for (int i = 0; i < kBN; ++i) {
-        float v = x[i] * sl2;
-        if (masked && key0 + i > qpos) v = -CUDART_INF_F;
-        x[i] = v;
-        mx = fmaxf(mx, v);
-      }
+      mx *= sl2;
       float corr = 1.f;
       bool rescale = false;
       if (mx > m_used + kRescaleLog2 || m_used == -CUDART_INF_F) {
         const float m_new = mx == -CUDART_INF_F ? 0.f : mx;
-        corr = exp2f(m_used - m_new);  // 0 while nothing has been accumulated
+        corr = ex2_approx(m_used - m_new);  // 0 while nothing has been accumulated
         rescale = j > 0 && m_used != -CUDART_INF_F;
         m_used = m_new;
       }
-      float psum = 0.f;
+      // pass 2: p = 2^(s*scale*log2e - m), packed f16 pairs over S's first 64 columns
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < kBN; ++i) {
-        x[i] = exp2f(x[i] - m_used);  // p, in place
-        psum += x[i];
+      for (int c = 0; c < kBN / 32; ++c) {
+        float v[32];
+        tmem_ld32(lane_addr + s_col + c * 32, v);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const bool d0 = masked && key0 + c * 32 + i > qpos;
+          const bool d1 = masked && key0 + c * 32 + i + 1 > qpos;
+          const float p0 = d0 ? 0.f : ex2_approx(fmaf(v[i], sl2, -m_used));
+          const float p1 = d1 ? 0.f : ex2_approx(fmaf(v[i + 1], sl2, -m_used));
+          ps[(i >> 1) & 3] += p0 + p1;
+          __half2 hp = __floats2half2_rn(p0, p1);
+          pk[i >> 1] = *reinterpret_cast<uint32_t*>(&hp);
+        }
+        tmem_st16(lane_addr + s_col + c * 16, pk);
       }
-      l = l * corr + psum;
-      if (j > 0 && !mbar_wait(pv_done, (j - 1) & 1, a.status)) {
-        ok = false;
-        break;
-      }
-      if (rescale) {
-        tc_fence_after();
+      l = l * corr + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+      if (rescale) {  // the previous P_q.V is complete: S_q(j) was issued after it
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
           float v[32];
-          tmem_ld32(lane_addr + C::kOCol + c * 32, v);
+          tmem_ld32(lane_addr + o_col + c * 32, v);
           tmem_wait_ld();
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] *= corr;
-          tmem_st32(lane_addr + C::kOCol + c * 32, v);
+          tmem_st32(lane_addr + o_col + c * 32, v);
         }
-        tmem_wait_st();
       }
-      // P row (f16): 16 chunks of 8 keys, chunk c of key half c/8 at its swizzled slot.
-#pragma unroll
-      for (int c = 0; c < kBN / 8; ++c) {
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          __half2 hp = __floats2half2_rn(x[8 * c + 2 * e], x[8 * c + 2 * e + 1]);
-          w[e] = *reinterpret_cast<uint32_t*>(&hp);
-        }
-        const uint32_t off = (c >> 3) * (kBM * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4);
-        *reinterpret_cast<uint4*>(psm + off) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[q]);
     }
     // ---- epilogue: O / l for the valid rows
-    if (ok && mbar_wait(pv_done, (n_kv - 1) & 1, a.status)) {
+    if (ok && mbar_wait(o_done, 0, a.status)) {
       tc_fence_after();
       const float inv = 1.f / l;
       const size_t obase = ((static_cast<size_t>(b) * a.new_len + row) * a.hq + h) * HD;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         float v[32];
-        tmem_ld32(lane_addr + C::kOCol + c * 32, v);
+        tmem_ld32(lane_addr + o_col + c * 32, v);
         tmem_wait_ld();
         if (row < a.new_len) {
           if (a.out_dtype == kF32) {
@@ -389,8 +426,17 @@ __global__ void __launch_bounds__(256, 1)
               o4[i] = make_float4(v[4 * i] * inv, v[4 * i + 1] * inv, v[4 * i + 2] * inv,
                                   v[4 * i + 3] * inv);
           } else {
+            uint4* o4 = reinterpret_cast<uint4*>(static_cast<uint16_t*>(a.out) + obase + c * 32);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) store_elem(a.out, obase + c * 32 + i, a.out_dtype, v[i] * inv);
+            for (int i = 0; i < 4; ++i) {
+              uint32_t w4[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float x0 = v[8 * i + 2 * e] * inv, x1 = v[8 * i + 2 * e + 1] * inv;
+                w4[e] = a.out_dtype == kF16 ? pack2<false>(x0, x1) : pack2<true>(x0, x1);
+              }
+              o4[i] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
           }
         }
       }
@@ -434,23 +480,22 @@ bool prefill_tc_supported(int hd, int dtype, int new_len) {
 
 size_t prefill_q_rows(int new_len) { return static_cast<size_t>((new_len + kBM - 1) / kBM) * kBM; }
 
-cudaError_t launch_prefill_tc(const PrefillArgs& a, const CUtensorMap* qmap,
-                              const CUtensorMap* kmap, const CUtensorMap* vmap, cudaStream_t s) {
-  using C = PrefillCfg<128>;
-  const int rows = a.batch * a.new_len * a.hq;
-  rope_q_kernel<<<(rows + 3) / 4, 128, 0, s>>>(a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+template <int NQ>
+static cudaError_t launch_prefill_nq(const PrefillArgs& a, const CUtensorMap* qmap,
+                                     const CUtensorMap* kmap, const CUtensorMap* vmap,
+                                     cudaStream_t s) {
+  using C = PrefillCfg<128, NQ>;
   static bool configured = false;
   if (!configured) {
-    e = cudaFuncSetAttribute(prefill_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(C::kSmem));
+    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<128, NQ>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(C::kSmem));
     if (e != cudaSuccess) return e;
     configured = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.new_len + kBM - 1) / kBM, a.hq, a.batch);
-  cfg.blockDim = dim3(256);
+  cfg.gridDim = dim3((a.new_len + kBM - 1) / kBM, a.hq / NQ, a.batch);
+  cfg.blockDim = dim3(C::kThreads);
   cfg.dynamicSmemBytes = C::kSmem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -458,7 +503,18 @@ cudaError_t launch_prefill_tc(const PrefillArgs& a, const CUtensorMap* qmap,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, prefill_tc_kernel<128>, a, *qmap, *kmap, *vmap);
+  return cudaLaunchKernelEx(&cfg, prefill_tc_kernel<128, NQ>, a, *qmap, *kmap, *vmap);
+}
+
+cudaError_t launch_prefill_tc(const PrefillArgs& a, const CUtensorMap* qmap,
+                              const CUtensorMap* kmap, const CUtensorMap* vmap, cudaStream_t s) {
+  const int rows = a.batch * a.new_len * a.hq;
+  rope_q_kernel<<<(rows + 3) / 4, 128, 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // Two heads of one KV group per CTA when the group has an even size.
+  if (a.group % 2 == 0) return launch_prefill_nq<2>(a, qmap, kmap, vmap, s);
+  return launch_prefill_nq<1>(a, qmap, kmap, vmap, s);
 }
 
 }  // namespace ql
