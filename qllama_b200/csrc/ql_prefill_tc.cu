@@ -152,6 +152,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
       "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
       : "memory");
 }
+// Register rebalancing between warpgroups.  The block launches with
+// kThreads x 168 registers; the TMA/MMA warpgroup gives back down to 64 and
+// each softmax warpgroup takes up to 216: 128*64 + 256*216 = 63488 <= 64512.
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {  // 2^x; -inf -> +0
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -239,6 +251,8 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   griddep_wait();
 
+  if (warp < 4) {
+  if constexpr (NQ == 2) regs_dec<64>();
   if (warp == 0) {
     // -------------------------------------------------------- producer --
     if (lane == 0) {
@@ -328,7 +342,9 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
       }
       tc_commit(o_done);
     }
-  } else if (warp >= 4) {
+  }
+  } else {
+    if constexpr (NQ == 2) regs_inc<216>();
     // --------------------------------------------------------- softmax --
     const int q = (warp - 4) >> 2;     // which query tile this warpgroup serves
     const int r = threadIdx.x & 127;   // row in the tile == TMEM lane
@@ -347,22 +363,29 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
       }
       tc_fence_after();
       const int key0 = j * kBN;
-      const bool masked = key0 + kBN - 1 > qpos;
-      // pass 1: row max of the scaled scores
-      float mx = -CUDART_INF_F;
+      // The whole S row in registers: four loads, one wait.
+      float x[kBN];
 #pragma unroll
       for (int c = 0; c < kBN / 32; ++c) {
         float v[32];
         tmem_ld32(lane_addr + s_col + c * 32, v);
-        tmem_wait_ld();
-        float m4[4] = {-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F};
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const bool dead = masked && key0 + c * 32 + i > qpos;
-          m4[i & 3] = fmaxf(m4[i & 3], dead ? -CUDART_INF_F : v[i]);
-        }
-        mx = fmaxf(mx, fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])));
+        for (int i = 0; i < 32; ++i) x[c * 32 + i] = v[i];
       }
+      tmem_wait_ld();
+      if (key0 + kBN - 1 > qpos) {  // diagonal tile: keys after this row's position are masked
+        const int lim = qpos - key0;  // keys 0..lim visible
+#pragma unroll
+        for (int i = 0; i < kBN; ++i)
+          if (i > lim) x[i] = -CUDART_INF_F;
+      }
+      float m8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) m8[e] = x[e];
+#pragma unroll
+      for (int i = 8; i < kBN; ++i) m8[i & 7] = fmaxf(m8[i & 7], x[i]);
+      float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                       fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       mx *= sl2;
       float corr = 1.f;
       bool rescale = false;
@@ -372,20 +395,15 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
         rescale = j > 0 && m_used != -CUDART_INF_F;
         m_used = m_new;
       }
-      // pass 2: p = 2^(s*scale*log2e - m), packed f16 pairs over S's first 64 columns
+      // p = 2^(s*scale*log2e - m), packed f16 pairs over S's first 64 columns
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < kBN / 32; ++c) {
-        float v[32];
-        tmem_ld32(lane_addr + s_col + c * 32, v);
-        tmem_wait_ld();
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 32; i += 2) {
-          const bool d0 = masked && key0 + c * 32 + i > qpos;
-          const bool d1 = masked && key0 + c * 32 + i + 1 > qpos;
-          const float p0 = d0 ? 0.f : ex2_approx(fmaf(v[i], sl2, -m_used));
-          const float p1 = d1 ? 0.f : ex2_approx(fmaf(v[i + 1], sl2, -m_used));
+          const float p0 = ex2_approx(fmaf(x[c * 32 + i], sl2, -m_used));
+          const float p1 = ex2_approx(fmaf(x[c * 32 + i + 1], sl2, -m_used));
           ps[(i >> 1) & 3] += p0 + p1;
           __half2 hp = __floats2half2_rn(p0, p1);
           pk[i >> 1] = *reinterpret_cast<uint32_t*>(&hp);
