@@ -268,6 +268,62 @@ int check_status(ql_ctx* c) {
   return QL_OK;
 }
 
+// Split plan of the split-KV decode kernel: the 64-position tiles each CTA
+// streams, and the most splits any (token, KV head) job is cut into.
+struct SplitPlan {
+  int tps;
+  int splits;
+};
+
+// tiles[b]: the most tiles a token of batch row b sees; per_row: the (token,
+// KV head) jobs of each row; slots: CTAs the whole GPU holds at once.
+// 1. While the jobs alone do not fill the slots twice, the KV length is split
+//    so that they do, keeping at least kMinSplitTiles tiles per split (a split
+//    of one or two tiles costs more to merge than it saves) and at most
+//    kMaxSplits splits; then the splits are evened out.
+// 2. Equal CTAs finish together, so a last wave that leaves slots idle is time
+//    lost.  While it would leave more than a tenth of them idle, up to four
+//    times as many splits are tried; the first that fills 90% is kept, else
+//    the fullest.
+SplitPlan plan_splits(const std::vector<int>& tiles, long long per_row, long long slots) {
+  constexpr int kMinSplitTiles = 4, kMaxSplits = 64;
+  int max_tiles = 1;
+  long long total = 0;
+  for (int t : tiles) {
+    max_tiles = std::max(max_tiles, t);
+    total += t * per_row;
+  }
+  const long long jobs = per_row * static_cast<long long>(tiles.size());
+  slots = std::max(1LL, slots);
+  int tps = max_tiles;
+  if (jobs < 2 * slots) {
+    tps = static_cast<int>(std::max(1LL, (total + 2 * slots - 1) / (2 * slots)));
+    tps = std::max(tps, kMinSplitTiles);
+    tps = std::max(tps, (max_tiles + kMaxSplits - 1) / kMaxSplits);
+  }
+  int splits = (max_tiles + tps - 1) / tps;
+  tps = (max_tiles + splits - 1) / splits;
+  auto fill = [&](int t) {
+    long long ctas = 0;
+    for (int x : tiles) ctas += (x + t - 1) / t * per_row;
+    const long long waves = (ctas + slots - 1) / slots;
+    return static_cast<double>(ctas) / static_cast<double>(waves * slots);
+  };
+  SplitPlan plan{tps, splits};
+  double best = fill(tps);
+  for (int sp = splits + 1; best < 0.9 && sp <= std::min(kMaxSplits, 4 * splits); ++sp) {
+    const int t = (max_tiles + sp - 1) / sp;
+    if (t < kMinSplitTiles) break;
+    if ((max_tiles + t - 1) / t != sp) continue;  // the same split as a smaller count
+    const double f = fill(t);
+    if (f > best) {
+      best = f;
+      plan = {t, sp};
+    }
+  }
+  return plan;
+}
+
 }  // namespace
 
 // ---------------------------------------------------- no-allocation decode --
@@ -719,30 +775,21 @@ int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
                           ql::prefill_tc_supported(hd, kv->cfg.dtype, n);
   // split planning for the tensor-core kernel
   int max_tiles = 0;
-  long long total_tiles = 0;
   int max_len = 0;
+  std::vector<int> row_tiles(a->batch);
   for (int b = 0; b < a->batch; ++b) {
     const int64_t end = ends[b];
     max_len = std::max<int>(max_len, static_cast<int>(end));
-    const int tl = static_cast<int>((end + ql::kTile - 1) / ql::kTile);
-    max_tiles = std::max(max_tiles, tl);
-    total_tiles += static_cast<long long>(tl) * n * hkv;  // upper bound over the batch's tokens
+    row_tiles[b] = static_cast<int>((end + ql::kTile - 1) / ql::kTile);
+    max_tiles = std::max(max_tiles, row_tiles[b]);
   }
   int tps = max_tiles, max_splits = 1;
   if (fast) {
-    // Split the KV length when there are too few (token, KV head) jobs to
-    // cover the GPU twice, keeping at least kMinSplitTiles tiles per split
-    // (a split of one or two tiles costs more to merge than it saves) and at
-    // most 64 splits; then even the splits out.
-    constexpr int kMinSplitTiles = 4;
-    const long long slots = 2LL * c->num_sms;
-    if (static_cast<long long>(jobs) * hkv < 2 * slots) {
-      tps = static_cast<int>(std::max<long long>(1, (total_tiles + 2 * slots - 1) / (2 * slots)));
-      tps = std::max(tps, kMinSplitTiles);
-      tps = std::max(tps, (max_tiles + 63) / 64);
-    }
-    max_splits = (max_tiles + tps - 1) / tps;
-    tps = (max_tiles + max_splits - 1) / max_splits;
+    const int per_sm = std::max(1, ql::splitkv_ctas_per_sm(hd, kv->cfg.dtype, false));
+    const SplitPlan plan =
+        plan_splits(row_tiles, static_cast<long long>(n) * hkv, 1LL * per_sm * c->num_sms);
+    tps = plan.tps;
+    max_splits = plan.splits;
   }
   // workspace: [staged q][k][v][out][part_o][part_ml][generic scratch f32][f64]
   size_t off = 0;
@@ -916,7 +963,7 @@ int ql_attn_decode_noalloc(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   std::vector<int64_t> ends(a->batch);
   std::vector<char> seen(kv->cfg.max_batch, 0);
   int max_tiles = 0;
-  long long total_tiles = 0;
+  std::vector<int> row_tiles(a->batch);
   for (int b = 0; b < a->batch; ++b) {
     const int s = a->seq_ids[b];
     if (s < 0 || s >= kv->cfg.max_batch)
@@ -936,9 +983,8 @@ int ql_attn_decode_noalloc(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
                   (long long)start, kv->cfg.max_seq_len);
     seqs[b] = s;
     ends[b] = start + 1;
-    const int tl = static_cast<int>((ends[b] + ql::kTile - 1) / ql::kTile);
-    max_tiles = std::max(max_tiles, tl);
-    total_tiles += static_cast<long long>(tl) * hkv;
+    row_tiles[b] = static_cast<int>((ends[b] + ql::kTile - 1) / ql::kTile);
+    max_tiles = std::max(max_tiles, row_tiles[b]);
   }
   QL_CUDA(cudaSetDevice(c->device), "set device");
   char* scratch = nullptr;
@@ -948,12 +994,8 @@ int ql_attn_decode_noalloc(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   if (r != QL_OK) return r;
   // Split plan of ql_attn_forward, with fewer splits if the partials would not fit.
   const int jobs = a->batch;
-  const long long slots = 2LL * c->num_sms;
-  int tps = max_tiles;
-  if (static_cast<long long>(jobs) * hkv < 2 * slots) {
-    tps = static_cast<int>(std::max<long long>(1, (total_tiles + 4 * slots - 1) / (4 * slots)));
-    tps = std::max(tps, (max_tiles + 63) / 64);
-  }
+  const int per_sm = std::max(1, ql::splitkv_ctas_per_sm(hd, kv->cfg.dtype, true));
+  int tps = plan_splits(row_tiles, hkv, 1LL * per_sm * c->num_sms).tps;
   auto part_bytes = [&](int splits) {
     return align256(static_cast<size_t>(jobs) * hkv * splits * 8 * 2 * sizeof(float)) +
            static_cast<size_t>(jobs) * hkv * splits * 8 * hd * sizeof(float);

@@ -20,6 +20,8 @@
 //  gather_kernel    KvCache::get (cache.rs:185-229) into f32.
 #include <math_constants.h>
 
+#include <atomic>
+
 #include "ql_device.cuh"
 #include "ql_kernels.cuh"
 
@@ -284,7 +286,9 @@ struct SplitCfg {
   static constexpr int kScaleBytes = kQ8 ? kTile * (HD / 32) * 2 : 0;
   static constexpr int kRaw = 2 * kKBytes + 2 * kScaleBytes;
   static constexpr int kStageBytes = (kRaw + 1023) / 1024 * 1024;
-  static constexpr int kStages = kQ8 ? 5 : (HD == 128 ? 3 : 6);
+  // Q8_0 keeps three stages so that three CTAs (15 warps) fit on an SM.
+  static constexpr int kStages = kQ8 ? 3 : (HD == 128 ? 3 : 6);
+  static constexpr int kMinCtas = kQ8 ? 3 : 2;  // resident CTAs per SM the registers allow
   static constexpr int kTx = kRaw;
   static constexpr int kQLd = HD + 8;  // q tile row stride (elements), padded
   static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes +
@@ -315,7 +319,7 @@ __device__ __forceinline__ void bar_consumers() {
 }  // namespace
 
 template <int HD, int DT, bool DEVROPE>
-__global__ void __launch_bounds__(160, 2)
+__global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
     splitkv_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, int job0) {
   using C = SplitCfg<HD, DT>;
@@ -448,12 +452,16 @@ __global__ void __launch_bounds__(160, 2)
   bar_consumers();
 
   // ----------------------------------------------------------- consumers --
-  uint32_t qa[NKS][4];
+  // A fragments of q: k-step ks starts 32 bytes after k-step ks-1.  The f16
+  // and bf16 variants hold all of them in registers; Q8_0, whose int8
+  // conversion needs the registers, reloads each one from shared memory.
+  const uint32_t qaddr =
+      smem_u32(qs + (((lane >> 3) & 1) * 8 + (lane & 7)) * C::kQLd + (lane >> 4) * 8);
+  uint32_t qa[Q8 ? 1 : NKS][4];
+  if constexpr (!Q8) {
 #pragma unroll
-  for (int ks = 0; ks < NKS; ++ks) {
-    const int r = ((lane >> 3) & 1) * 8 + (lane & 7);
-    const int col = ks * 16 + (lane >> 4) * 8;
-    ldmatrix_x4(smem_u32(qs + r * C::kQLd + col), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+    for (int ks = 0; ks < NKS; ++ks)
+      ldmatrix_x4(qaddr + ks * 32, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
   }
 
   float o[NO][4];
@@ -494,6 +502,8 @@ __global__ void __launch_bounds__(160, 2)
           float sb2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
           for (int s2 = 0; s2 < 2; ++s2) {
+            uint32_t qf[4];
+            ldmatrix_x4(qaddr + (2 * blk + s2) * 32, qf[0], qf[1], qf[2], qf[3]);
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
               const int r = 16 * warp + 8 * nt + g;
@@ -502,7 +512,7 @@ __global__ void __launch_bounds__(160, 2)
                   *reinterpret_cast<const uint32_t*>(sb + swz128(r, byte >> 4) + (byte & 15));
               uint32_t b0, b1;
               i8x4_to_h2x2(w, b0, b1);
-              mma16816<false>(sb2[nt], qa[2 * blk + s2], b0, b1);
+              mma16816<false>(sb2[nt], qf, b0, b1);
             }
           }
 #pragma unroll
@@ -550,12 +560,16 @@ __global__ void __launch_bounds__(160, 2)
       }
       l = l * corr + psum;
       m = m_new;
+      // corr is exactly 1 while the running maximum stays put, the usual case
+      // past the first tiles; the warp then skips the rescale.
+      if (__any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
-      for (int j = 0; j < NO; ++j) {
-        o[j][0] *= corr;
-        o[j][1] *= corr;
-        o[j][2] *= corr;
-        o[j][3] *= corr;
+        for (int j = 0; j < NO; ++j) {
+          o[j][0] *= corr;
+          o[j][1] *= corr;
+          o[j][2] *= corr;
+          o[j][3] *= corr;
+        }
       }
       // P as the A operand: row g = high part, row g+8 = remainder.
       constexpr bool PBF = BF;  // Q8_0 dequantises V to f16
@@ -726,18 +740,39 @@ bool splitkv_supported(int hd, int dtype, int group, int page) {
   return (dtype == kF16 || dtype == kBF16) && (hd == 64 || hd == 128);
 }
 
+// Sets the kernel's shared-memory limit on the current device (once per
+// device) and reports how many of its CTAs an SM holds.
+template <int HD, int DT, bool DEVROPE>
+static cudaError_t configure_splitkv_t(int* ctas_per_sm) {
+  using C = SplitCfg<HD, DT>;
+  constexpr int kMaxDev = 64;
+  static std::atomic<int> occupancy[kMaxDev];  // 0 = not configured yet
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < kMaxDev && occupancy[dev].load(std::memory_order_acquire) > 0) {
+    if (ctas_per_sm) *ctas_per_sm = occupancy[dev].load(std::memory_order_relaxed);
+    return cudaSuccess;
+  }
+  e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmem));
+  if (e != cudaSuccess) return e;
+  int n = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, splitkv_kernel<HD, DT, DEVROPE>, 160,
+                                                    C::kSmem);
+  if (e != cudaSuccess) return e;
+  n = max(n, 1);
+  if (dev < kMaxDev) occupancy[dev].store(n, std::memory_order_release);
+  if (ctas_per_sm) *ctas_per_sm = n;
+  return cudaSuccess;
+}
+
 template <int HD, int DT, bool DEVROPE>
 static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
                                     const CUtensorMap* vmap, int jobs, cudaStream_t s, bool pdl) {
   using C = SplitCfg<HD, DT>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(C::kSmem));
-    if (e != cudaSuccess) return e;
-    configured = true;
-  }
+  cudaError_t e = configure_splitkv_t<HD, DT, DEVROPE>(nullptr);
+  if (e != cudaSuccess) return e;
   for (int j0 = 0; j0 < jobs; j0 += 65535) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.max_splits, a.cache.hkv, min(65535, jobs - j0));
@@ -749,7 +784,7 @@ static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE>, a, *kmap, *vmap, j0);
+    e = cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE>, a, *kmap, *vmap, j0);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
@@ -765,6 +800,25 @@ static cudaError_t dispatch_splitkv(const AttnArgs& a, const CUtensorMap* kmap,
                        : launch_splitkv_t<128, kF16, DEVROPE>(a, kmap, vmap, jobs, s, pdl);
   return dt == kBF16 ? launch_splitkv_t<64, kBF16, DEVROPE>(a, kmap, vmap, jobs, s, pdl)
                      : launch_splitkv_t<64, kF16, DEVROPE>(a, kmap, vmap, jobs, s, pdl);
+}
+
+template <bool DEVROPE>
+static int ctas_per_sm_t(int hd, int dt) {
+  int n = 0;
+  cudaError_t e;
+  if (dt == kQ8_0)
+    e = configure_splitkv_t<128, kQ8_0, DEVROPE>(&n);
+  else if (hd == 128)
+    e = dt == kBF16 ? configure_splitkv_t<128, kBF16, DEVROPE>(&n)
+                    : configure_splitkv_t<128, kF16, DEVROPE>(&n);
+  else
+    e = dt == kBF16 ? configure_splitkv_t<64, kBF16, DEVROPE>(&n)
+                    : configure_splitkv_t<64, kF16, DEVROPE>(&n);
+  return e == cudaSuccess ? n : 0;
+}
+
+int splitkv_ctas_per_sm(int hd, int dtype, bool device_rope) {
+  return device_rope ? ctas_per_sm_t<true>(hd, dtype) : ctas_per_sm_t<false>(hd, dtype);
 }
 
 cudaError_t launch_splitkv(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,

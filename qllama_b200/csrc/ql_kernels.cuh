@@ -108,6 +108,9 @@ struct GatherArgs {
 size_t splitkv_smem_bytes(int hd, int dtype);
 // Whether the split-KV tensor-core kernel handles this configuration.
 bool splitkv_supported(int hd, int dtype, int group, int page);
+// Resident CTAs per SM of the split-KV kernel for a configuration on the
+// current device (0 if the query failed); configures the kernel as well.
+int splitkv_ctas_per_sm(int hd, int dtype, bool device_rope);
 
 cudaError_t launch_append(const AppendArgs& a, cudaStream_t s);
 cudaError_t launch_splitkv(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,

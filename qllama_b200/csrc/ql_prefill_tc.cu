@@ -355,14 +355,29 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
     const uint32_t s_col = q * kBN, o_col = C::kOCol + q * 128;
     const float sl2 = a.scale * kLog2eP;
     float m_used = -CUDART_INF_F, l = 0.f;
+    // tcgen05.ld/st are warp-collective (.sync.aligned): every branch around
+    // them below is taken by whole warps, decided with warp votes.
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!mbar_wait(&s_full[q], j & 1, a.status)) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[q], j & 1, a.status))) {
         ok = false;
         break;
       }
       tc_fence_after();
       const int key0 = j * kBN;
+      if (q == 0 && j == n_kv - 1 && key0 + r >= kv_end) {
+        // Key r of the last tile lies past the sequence end: its V row may be
+        // stale pool memory (Inf/NaN), and P = 0 times Inf would still reach
+        // O.  Zero it before the PV MMAs read it (V landed before S_0 was
+        // issued; every PV of this tile is issued after P_0 is released).
+        uint8_t* vrow = stg + (j & 1) * C::kStageBytes + C::kKBytes + r * 128;
+#pragma unroll
+        for (int hf = 0; hf < C::kHalves; ++hf)
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<uint4*>(vrow + hf * (kBN * 128) + c * 16) = make_uint4(0, 0, 0, 0);
+        fence_proxy_async_smem();
+      }
       // The whole S row in registers: four loads, one wait.
       float x[kBN];
 #pragma unroll
@@ -395,6 +410,9 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
         rescale = j > 0 && m_used != -CUDART_INF_F;
         m_used = m_new;
       }
+      // The warp rescales its O rows together; rows that kept their maximum
+      // multiply by exactly 1.
+      rescale = __any_sync(0xffffffffu, rescale);
       // p = 2^(s*scale*log2e - m), packed f16 pairs over S's first 64 columns
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -427,7 +445,7 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
       mbar_arrive(&p_full[q]);
     }
     // ---- epilogue: O / l for the valid rows
-    if (ok && mbar_wait(o_done, 0, a.status)) {
+    if (__all_sync(0xffffffffu, ok && mbar_wait(o_done, 0, a.status))) {
       tc_fence_after();
       const float inv = 1.f / l;
       const size_t obase = ((static_cast<size_t>(b) * a.new_len + row) * a.hq + h) * HD;
@@ -470,20 +488,27 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
 }
 
 // ------------------------------------------------------ rotated-Q scratch --
-// One warp per (sequence, token, query head): RoPE with the host table (bit
+// One warp per (sequence, query row, query head), padding rows of the last
+// 128-row tile included (written as zeros): RoPE with the host table (bit
 // for bit the reference's rotation), rounded to f16, at
 // q_out[((b*hq + h)*q_rows + t)*hd + d].
 __global__ void __launch_bounds__(128) rope_q_kernel(const __grid_constant__ PrefillArgs a) {
-  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const int rows = a.batch * a.new_len * a.hq;
+  const long long rows = static_cast<long long>(a.batch) * a.q_rows * a.hq;
   if (w >= rows) return;
-  const int h = w % a.hq, t = (w / a.hq) % a.new_len, b = w / (a.hq * a.new_len);
+  const int h = static_cast<int>(w % a.hq), t = static_cast<int>((w / a.hq) % a.q_rows);
+  const int b = static_cast<int>(w / (static_cast<long long>(a.hq) * a.q_rows));
   const int hd = a.cache.hd;
+  __half* out = a.q_rot + ((static_cast<size_t>(b) * a.hq + h) * a.q_rows + t) * hd;
+  if (t >= a.new_len) {  // padding rows of the last query tile: zeros, never stale memory
+    for (int p = lane; p < hd / 2; p += 32)
+      *reinterpret_cast<__half2*>(out + 2 * p) = __floats2half2_rn(0.f, 0.f);
+    return;
+  }
   const int pos = a.seqs.start[b] + t;
   const double2* rr = a.rope + static_cast<size_t>(pos) * (hd / 2);
   const size_t in = (static_cast<size_t>(b * a.new_len + t) * a.hq + h) * hd;
-  __half* out = a.q_rot + ((static_cast<size_t>(b) * a.hq + h) * a.q_rows + t) * hd;
   for (int p = lane; p < hd / 2; p += 32) {
     float y0, y1;
     rope_pair(load_elem(a.q, in + 2 * p, a.in_dtype), load_elem(a.q, in + 2 * p + 1, a.in_dtype),
@@ -526,8 +551,8 @@ static cudaError_t launch_prefill_nq(const PrefillArgs& a, const CUtensorMap* qm
 
 cudaError_t launch_prefill_tc(const PrefillArgs& a, const CUtensorMap* qmap,
                               const CUtensorMap* kmap, const CUtensorMap* vmap, cudaStream_t s) {
-  const int rows = a.batch * a.new_len * a.hq;
-  rope_q_kernel<<<(rows + 3) / 4, 128, 0, s>>>(a);
+  const long long rows = static_cast<long long>(a.batch) * a.q_rows * a.hq;
+  rope_q_kernel<<<static_cast<unsigned>((rows + 3) / 4), 128, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   // Two heads of one KV group per CTA when the group has an even size.
