@@ -84,6 +84,23 @@ def peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def ncu_traffic(workload, batch, alg_bytes):
+    """DRAM bytes per launch of the dominant kernel, scaled from the small-case
+    ncu capture in profiles/dram_traffic.txt (None when there is none)."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        f = line.split()
+        if not f or f[0].startswith("#") or f[0] != workload:
+            continue
+        case_batch, rd, wr, case_alg = int(f[2]), float(f[3]), float(f[4]), float(f[5])
+        if WORKLOADS[workload]["kind"] == "prefill":
+            return (rd + wr) * batch / case_batch
+        return (rd + wr) / case_alg * alg_bytes
+    return None
+
+
 def seq_lengths(w, rank=0):
     """Cached lengths of the sequences before the first decode step (seeded)."""
     if w["kind"] != "decode":
@@ -412,7 +429,8 @@ def run_ours(args, w):
         achieved = pre_flops / t_pre / 1e12
         roof = {"kernel": "prefill_tc_kernel<128> (tcgen05/TMEM causal attention)",
                 "bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
-                "frac": achieved / bf16, "peak_source": which, "traffic": None,
+                "frac": achieved / bf16, "peak_source": which,
+                "traffic": ncu_traffic(args.workload, B, None),
                 "flops_per_launch": pre_flops / Lyr, "launch_us": 1e6 * t_pre / Lyr,
                 "timed": "the whole call: append, rotated-q and attention kernels"}
     else:
@@ -420,7 +438,8 @@ def run_ours(args, w):
         achieved = dec_bytes / t_dec / 1e9
         roof = {"kernel": f"splitkv_kernel<{hd},{w['kv']}> (fused RoPE+append+decode attention)",
                 "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                "frac": achieved / hbm, "peak_source": which, "traffic": None,
+                "frac": achieved / hbm, "peak_source": which,
+                "traffic": ncu_traffic(args.workload, B, dec_bytes / (D * Lyr)),
                 "bytes_per_launch": dec_bytes / (D * Lyr), "launch_us": 1e6 * t_dec / (D * Lyr),
                 "timed": "decode phase / launches, graph gaps included"}
     if rank == 0:
@@ -474,8 +493,16 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the workload's batch (a smaller case of the same shapes, "
+                         "e.g. for an ncu capture; the line then names the changed config)")
+    ap.add_argument("--layers", type=int, default=None, help="override the layer count")
     args = ap.parse_args()
-    w = WORKLOADS[args.workload]
+    w = dict(WORKLOADS[args.workload])
+    for key in ("batch", "layers"):
+        if getattr(args, key) is not None:
+            w[key] = getattr(args, key)
+            w["desc"] += f" [{key} overridden to {w[key]}]"
     if args.impl == "reference":
         run_reference(args, w)
     else:

@@ -309,6 +309,38 @@ def test_tcgen05_prefill_parity(ctx, batch, n, start, hq, hkv):
     assert gu.max_err(out1, ref1) <= TOL_16
 
 
+def test_tcgen05_prefill_ignores_stale_rows_past_the_end(ctx):
+    """Pages keep old rows after a roll-back; keys past the end must not reach O.
+
+    Positions 0..255 are first written with Inf/NaN K and V and rolled back,
+    so the last 128-key tile of a 200-token prefill reads them (keys 200..255)
+    from the same pages. Their probabilities are exactly 0, and 0 * Inf must
+    not turn the visible rows into NaN."""
+    rng = np.random.default_rng(23)
+    hd, hq, hkv, theta, n = 128, 8, 2, 500000.0, 200
+    p = gu.Pair(ctx, "f16", 1, 320, hkv, hd, 1)
+    bad = np.full((256, hkv, hd), np.inf, np.float32)
+    bad[:, :, 1::3] = np.nan
+    bad[:, :, 2::3] = -np.inf
+    p.gpu.update(0, bad, bad, np.arange(256))
+    p.gpu.truncate(0, 0)
+    assert p.gpu.seq_len(0) == 0
+    q, k, v = (gu.rounded(gu.normal(rng, (1, n, h, hd)), "bf16") for h in (hq, hkv, hkv))
+    out = qb.attention_forward(p.gpu, 0, gu.to_device(q, "bf16"), gu.to_device(k, "bf16"),
+                               gu.to_device(v, "bf16"), [0], hq, hkv, hd, theta)
+    p.gpu.ctx.synchronize()
+    ref = p.oracle_forward(0, q, k, v, [0], hq, theta)
+    assert np.isfinite(out.float().cpu().numpy()).all()
+    assert gu.max_err(out, ref) <= TOL_16
+    # the split-KV decode step reads the same stale tail (keys 201..255)
+    q1, k1, v1 = (gu.rounded(gu.normal(rng, (1, 1, h, hd)), "bf16") for h in (hq, hkv, hkv))
+    out1 = qb.attention_forward(p.gpu, 0, gu.to_device(q1, "bf16"), gu.to_device(k1, "bf16"),
+                                gu.to_device(v1, "bf16"), [n], hq, hkv, hd, theta)
+    ref1 = p.oracle_forward(0, q1, k1, v1, [n], hq, theta)
+    assert np.isfinite(out1.float().cpu().numpy()).all()
+    assert gu.max_err(out1, ref1) <= TOL_16
+
+
 def test_truncate_rolls_back_and_rewrites(ctx):
     """ql_kv_truncate: roll a sequence back, write new rows over the old positions."""
     rng = np.random.default_rng(21)
