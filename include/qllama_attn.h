@@ -193,6 +193,53 @@ int ql_attn_forward(ql_ctx* ctx, ql_kv* kv, const ql_attn_args* args);
 #define QL_NOALLOC_MAX_PAIRS 16384
 int ql_attn_decode_noalloc(ql_ctx* ctx, ql_kv* kv, const ql_attn_args* args);
 
+/* ---- head-sharded layers across GPUs ---------------------------------------
+ * No counterpart in the reference, a single-process CPU program.  A layer's
+ * KV heads are split evenly over `nranks` GPUs, one process per GPU: rank r
+ * owns KV heads [r*Hkv/n, (r+1)*Hkv/n) with their query heads, keeps its own
+ * ql_kv for them and receives only their Q/K/V.  ql_attn_forward_sharded
+ * computes the rank's heads and all-gathers the outputs, so every rank ends
+ * with the whole [batch, new_len, Hq*head_dim] in the layout of
+ * layers.rs:447-455 (rank r's heads in columns [r*Hq/n*hd, (r+1)*Hq/n*hd)).
+ *
+ * Exchange (QL_COMM_P2P): a single-token decode on the split-KV kernel stores
+ * each output row straight into every rank's output buffer over NVLink, from
+ * the attention kernel itself; the buffers are mapped between the processes
+ * with CUDA IPC when the communicator is created, and completion is signalled
+ * with flags whose waits are bounded.  Other calls compute locally, then a
+ * copy kernel pushes the rows the same way.  QL_COMM_NCCL selects the library
+ * baseline instead (ncclAllGather, then a rank-major to head-major permute).
+ * NCCL (libnccl.so.2) is loaded at ql_comm_create; nothing else needs it.
+ *
+ * Collective semantics: every rank makes the same sequence of sharded calls
+ * on the same shapes.  The ranks must issue each call within 5 seconds of one
+ * another; a rank that does not shows up as QL_ERR_DEVICE ("another GPU")
+ * at the next ql_ctx_synchronize.  q, k, v and out are device buffers.
+ */
+#define QL_COMM_ID_BYTES 128
+typedef struct {
+  char bytes[QL_COMM_ID_BYTES];
+} ql_comm_id;
+typedef struct ql_comm ql_comm;
+#define QL_COMM_P2P 0
+#define QL_COMM_NCCL 1
+#define QL_COMM_MAX_RANKS 8
+
+/* Made on one rank and handed to the others out of band (e.g. a broadcast). */
+int ql_comm_unique_id(ql_comm_id* out);
+/* Collective over the nranks processes; max_out_bytes bounds the whole output
+ * of one sharded call (batch*new_len*Hq*head_dim*element size). */
+int ql_comm_create(ql_ctx* ctx, int nranks, int rank, const ql_comm_id* id,
+                   uint64_t max_out_bytes, int mode, ql_comm** out);
+/* Collective; every rank's calls must have finished (ql_ctx_synchronize). */
+int ql_comm_destroy(ql_comm* comm);
+/* This rank's symmetric output buffer.  Passing it as args->out of a sharded
+ * call skips the final device-to-device copy. */
+int ql_comm_buffer(ql_comm* comm, void** out, uint64_t* bytes);
+/* args: num_heads / num_kv_heads are this rank's counts, q/k/v this rank's
+ * heads; out holds batch*new_len rows of num_heads*nranks*head_dim. */
+int ql_attn_forward_sharded(ql_ctx* ctx, ql_kv* kv, ql_comm* comm, const ql_attn_args* args);
+
 #ifdef __cplusplus
 }
 #endif

@@ -8,7 +8,10 @@ for this path:
   device resident and paged, with f32, f16, bf16 or Q8_0 storage and several
   sequence slots;
 * ``attention_forward`` -- steps 3-7 of ``Attention::forward_with_cache``
-  (src/transformer/layers.rs:397-455) on already projected Q/K/V.
+  (src/transformer/layers.rs:397-455) on already projected Q/K/V;
+* ``Comm`` / ``attention_forward_sharded`` -- the same operator with the KV
+  heads split over several GPUs (one process each) and the outputs
+  all-gathered into the reference's head-major layout (layers.rs:447-455).
 
 There is no CPU fallback: without the compiled library or a CUDA device the
 calls raise.
@@ -33,8 +36,14 @@ EXPORTS = (
     "ql_version", "ql_last_error", "ql_ctx_create", "ql_ctx_destroy", "ql_ctx_set_stream",
     "ql_ctx_synchronize", "ql_kv_create", "ql_kv_destroy", "ql_kv_clear", "ql_kv_clear_seq",
     "ql_kv_seq_len", "ql_kv_layer_len", "ql_kv_update", "ql_kv_get", "ql_attn_forward",
-    "ql_attn_decode_noalloc", "ql_kv_truncate",
+    "ql_attn_decode_noalloc", "ql_kv_truncate", "ql_comm_unique_id", "ql_comm_create",
+    "ql_comm_destroy", "ql_comm_buffer", "ql_attn_forward_sharded",
 )
+
+COMM_P2P, COMM_NCCL = 0, 1
+COMM_MODES = {"p2p": COMM_P2P, "nccl": COMM_NCCL}
+COMM_ID_BYTES = 128
+MAX_RANKS = 8
 
 
 class QllamaError(RuntimeError):
@@ -61,6 +70,10 @@ class AttnArgs(ctypes.Structure):
                 ("out_dtype", ctypes.c_int32), ("mem", ctypes.c_int32),
                 ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
                 ("out", ctypes.c_void_p)]
+
+
+class CommId(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_char * COMM_ID_BYTES)]
 
 
 _lib = None
@@ -101,6 +114,12 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
     L.ql_kv_get.argtypes = [vp, vp, i32, i32, i32p, i64, vp, vp, i32]
     L.ql_attn_forward.argtypes = [vp, vp, ctypes.POINTER(AttnArgs)]
     L.ql_attn_decode_noalloc.argtypes = [vp, vp, ctypes.POINTER(AttnArgs)]
+    L.ql_comm_unique_id.argtypes = [ctypes.POINTER(CommId)]
+    L.ql_comm_create.argtypes = [vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(CommId),
+                                 ctypes.c_uint64, ctypes.c_int, ctypes.POINTER(vp)]
+    L.ql_comm_destroy.argtypes = [vp]
+    L.ql_comm_buffer.argtypes = [vp, ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_uint64)]
+    L.ql_attn_forward_sharded.argtypes = [vp, vp, vp, ctypes.POINTER(AttnArgs)]
     for name in EXPORTS:
         if name not in ("ql_version", "ql_last_error"):
             getattr(L, name).restype = ctypes.c_int
@@ -240,16 +259,9 @@ class KvCache:
             pass
 
 
-def attention_forward(kv: KvCache, layer: int, q, k, v, start_pos, num_heads: int,
-                      num_kv_heads: int, head_dim: int, rope_theta: float, seq_ids=None,
-                      out=None, out_dtype: str | None = None):
-    """Steps 3-7 of Attention::forward_with_cache for a batch of sequences.
-
-    q: [batch, new_len, num_heads, head_dim] (or [new_len, H, hd] for one
-    sequence), k/v: [..., num_kv_heads, head_dim], pre-RoPE.  numpy arrays are
-    host buffers (copied in and out inside the call); torch CUDA tensors are
-    used in place.  Returns out [batch, new_len, num_heads*head_dim].
-    """
+def _attn_call(q, k, v, start_pos, num_heads, num_kv_heads, head_dim, rope_theta, layer,
+               seq_ids, out, out_dtype, out_heads):
+    """(AttnArgs, out, single, keep-alive) for one operator call."""
     single = len(q.shape) == 3
     if single:
         q, k, v = q[None], k[None], v[None]
@@ -264,7 +276,7 @@ def attention_forward(kv: KvCache, layer: int, q, k, v, start_pos, num_heads: in
     in_dt = _dtype_code(qq)
     od = DTYPES[out_dtype] if out_dtype else F32
     if out is None:
-        shape = (batch, new_len, num_heads * head_dim)
+        shape = (batch, new_len, out_heads * head_dim)
         if mem == MEM_HOST:
             out = np.empty(shape, {F32: np.float32, F16: np.float16}.get(od, np.float32))
             if od == BF16:
@@ -279,5 +291,84 @@ def attention_forward(kv: KvCache, layer: int, q, k, v, start_pos, num_heads: in
     args = AttnArgs(layer, batch, new_len, seqs.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
                     starts.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)), num_heads,
                     num_kv_heads, head_dim, rope_theta, in_dt, od, mem, qp, kp, vp, op)
+    return args, out, single, (qq, kk, vv, oo, starts, seqs)
+
+
+def attention_forward(kv: KvCache, layer: int, q, k, v, start_pos, num_heads: int,
+                      num_kv_heads: int, head_dim: int, rope_theta: float, seq_ids=None,
+                      out=None, out_dtype: str | None = None):
+    """Steps 3-7 of Attention::forward_with_cache for a batch of sequences.
+
+    q: [batch, new_len, num_heads, head_dim] (or [new_len, H, hd] for one
+    sequence), k/v: [..., num_kv_heads, head_dim], pre-RoPE.  numpy arrays are
+    host buffers (copied in and out inside the call); torch CUDA tensors are
+    used in place.  Returns out [batch, new_len, num_heads*head_dim].
+    """
+    args, out, single, keep = _attn_call(q, k, v, start_pos, num_heads, num_kv_heads, head_dim,
+                                         rope_theta, layer, seq_ids, out, out_dtype, num_heads)
     _check(load().ql_attn_forward(kv.ctx._h, kv._h, ctypes.byref(args)))
+    return out[0] if single else out
+
+
+# ------------------------------------------------------------ several GPUs --
+
+def shard_heads(num_heads: int, num_kv_heads: int, nranks: int, rank: int):
+    """(query-head range, KV-head range) rank `rank` owns when a layer's KV
+    heads are split evenly over `nranks` GPUs; each KV head keeps its group of
+    num_heads/num_kv_heads query heads (layers.rs:436)."""
+    if nranks < 1 or not 0 <= rank < nranks:
+        raise QllamaError(ERR_INVALID, f"rank {rank} is outside 0..{nranks - 1}")
+    if num_heads % num_kv_heads or num_kv_heads % nranks:
+        raise QllamaError(ERR_INVALID, f"{num_kv_heads} KV heads do not split evenly over "
+                                       f"{nranks} GPUs (or num_heads is not divisible)")
+    hkv = num_kv_heads // nranks
+    hq = hkv * (num_heads // num_kv_heads)
+    return range(rank * hq, (rank + 1) * hq), range(rank * hkv, (rank + 1) * hkv)
+
+
+def comm_unique_id() -> bytes:
+    """A fresh communicator id (made on one rank, handed to the others)."""
+    cid = CommId()
+    _check(load().ql_comm_unique_id(ctypes.byref(cid)))
+    return ctypes.string_at(ctypes.addressof(cid), COMM_ID_BYTES)  # all bytes, NULs included
+
+
+class Comm:
+    """ql_comm: this process's member of a head-sharded group of GPUs."""
+
+    def __init__(self, ctx: Context, nranks: int, rank: int, unique_id: bytes,
+                 max_out_bytes: int, mode: str = "p2p"):
+        if len(unique_id) != COMM_ID_BYTES:
+            raise QllamaError(ERR_INVALID, f"a communicator id has {COMM_ID_BYTES} bytes")
+        cid = CommId()
+        ctypes.memmove(ctypes.addressof(cid), bytes(unique_id), COMM_ID_BYTES)
+        h = ctypes.c_void_p()
+        _check(load().ql_comm_create(ctx._h, nranks, rank, ctypes.byref(cid), max_out_bytes,
+                                     COMM_MODES[mode], ctypes.byref(h)))
+        self._h, self.ctx, self.nranks, self.rank = h, ctx, nranks, rank
+
+    def buffer(self):
+        """(device pointer, bytes) of this rank's symmetric output buffer."""
+        p, n = ctypes.c_void_p(), ctypes.c_uint64()
+        _check(load().ql_comm_buffer(self._h, ctypes.byref(p), ctypes.byref(n)))
+        return p.value, n.value
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            h, self._h = self._h, None
+            _check(load().ql_comm_destroy(h))
+
+
+def attention_forward_sharded(comm: Comm, kv: KvCache, layer: int, q, k, v, start_pos,
+                              num_heads: int, num_kv_heads: int, head_dim: int,
+                              rope_theta: float, seq_ids=None, out=None,
+                              out_dtype: str | None = None):
+    """attention_forward over this rank's heads (num_heads / num_kv_heads are
+    the local counts), returning the whole layer's output
+    [batch, new_len, num_heads*nranks*head_dim] gathered from every rank.
+    Device tensors only; every rank makes the same calls."""
+    args, out, single, keep = _attn_call(q, k, v, start_pos, num_heads, num_kv_heads, head_dim,
+                                         rope_theta, layer, seq_ids, out, out_dtype,
+                                         num_heads * comm.nranks)
+    _check(load().ql_attn_forward_sharded(kv.ctx._h, kv._h, comm._h, ctypes.byref(args)))
     return out[0] if single else out

@@ -11,12 +11,15 @@
 // hold here too.  Sequence lengths advance only after the work is queued.
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <algorithm>
 #include <cstring>
+#include <memory>
 #include <string>
 #include <vector>
 
@@ -262,8 +265,10 @@ int check_status(ql_ctx* c) {
   if (st) {
     cudaMemset(c->status, 0, sizeof(uint32_t));
     return fail(QL_ERR_DEVICE, "a kernel reported status 0x%x (%s)", st,
-                (st & ql::kStatusWaitTimeout) ? "a pipeline wait timed out"
-                                              : "a block-table entry was out of range");
+                (st & ql::kStatusPeerTimeout)   ? "another GPU of a head-sharded call did not "
+                                                  "signal within the wait limit"
+                : (st & ql::kStatusWaitTimeout) ? "a pipeline wait timed out"
+                                                : "a block-table entry was out of range");
   }
   return QL_OK;
 }
@@ -689,7 +694,10 @@ int ql_kv_get(ql_ctx* c, const ql_kv* kv, int32_t layer, int32_t seq, const int3
   return QL_OK;
 }
 
-int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
+// The operator.  With `peer` (a head-sharded single-token decode), the
+// split-KV kernel stores its rows into every rank's output instead of a->out.
+static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
+                             const ql::PeerOut* peer) {
   if (!c || !kv || !a) return fail(QL_ERR_INVALID, "ql_attn_forward: NULL argument");
   const int hq = a->num_heads, hkv = a->num_kv_heads, hd = a->head_dim;
   // Attention::new (layers.rs:254-261)
@@ -759,6 +767,10 @@ int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   }
   if (n == 0) return QL_OK;  // empty batch (transformer_forward.rs:919-946)
   if (!a->q || !a->k || !a->v || !a->out) return fail(QL_ERR_INVALID, "q/k/v/out is NULL");
+  if (peer && !(n == 1 && a->mem == QL_MEM_DEVICE && kv->have_maps &&
+                ql::splitkv_supported(hd, kv->cfg.dtype, hq / hkv, kv->cfg.page_size)))
+    return fail(QL_ERR_UNSUPPORTED, "the fused head-sharded exchange needs a single-token "
+                "decode on the split-KV kernel");
   QL_CUDA(cudaSetDevice(c->device), "set device");
   int r = reserve_pages(kv, seqs, ends);
   if (r != QL_OK) return r;
@@ -902,8 +914,14 @@ int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   at.scratch = reinterpret_cast<float*>(w + o_gs);
   at.scratch_d = reinterpret_cast<double*>(w + o_gd);
   at.max_len = max_len;
+  at.out_vec = (reinterpret_cast<uintptr_t>(out) % 16) == 0;
   at.status = c->status;
   at.seqs = st;
+  if (peer) {
+    at.peer = *peer;
+    at.peer.total_ctas = max_splits * hkv * jobs;
+    at.out_vec = 1;  // symmetric buffers are 256-byte aligned
+  }
   if (fast)
     QL_CUDA(ql::launch_splitkv(at, &kv->kmap[layer], &kv->vmap[layer], jobs, c->stream),
             "launch split-KV attention");
@@ -916,6 +934,10 @@ int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   }
   for (int b = 0; b < a->batch; ++b) len_at(kv, layer, seqs[b]) = ends[b];
   return QL_OK;
+}
+
+int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
+  return attn_forward_impl(c, kv, a, nullptr);
 }
 
 int ql_attn_decode_noalloc(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
@@ -1035,6 +1057,7 @@ int ql_attn_decode_noalloc(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   at.part_o = part_o;
   at.part_ml = part_ml;
   at.counters = counters;
+  at.out_vec = (reinterpret_cast<uintptr_t>(a->out) % 16) == 0;
   at.status = c->status;
   for (int b = 0; b < a->batch; ++b) {
     at.seqs.seq[b] = seqs[b];
@@ -1048,3 +1071,275 @@ int ql_attn_decode_noalloc(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
 
 }  // extern "C"
 
+
+// ------------------------------------------------ head-sharded layers --
+// NCCL is opened on first use, so that single-GPU callers never need it.
+namespace {
+
+struct NcclApi {
+  bool ok = false;
+  std::string why;
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                             cudaStream_t) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+};
+
+const NcclApi& nccl_api() {
+  static const NcclApi api = [] {
+    NcclApi x;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      const char* e = dlerror();
+      x.why = e ? e : "dlopen failed";
+      return x;
+    }
+    x.get_unique_id = reinterpret_cast<decltype(x.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    x.comm_init_rank = reinterpret_cast<decltype(x.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    x.comm_destroy = reinterpret_cast<decltype(x.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    x.all_gather = reinterpret_cast<decltype(x.all_gather)>(dlsym(h, "ncclAllGather"));
+    x.error_string = reinterpret_cast<decltype(x.error_string)>(dlsym(h, "ncclGetErrorString"));
+    x.ok = x.get_unique_id && x.comm_init_rank && x.comm_destroy && x.all_gather && x.error_string;
+    if (!x.ok) x.why = "libnccl.so.2 lacks an entry point this library calls";
+    return x;
+  }();
+  return api;
+}
+
+int nccl_fail(ncclResult_t r, const char* what) {
+  return fail(QL_ERR_CUDA, "%s: %s", what, nccl_api().error_string(r));
+}
+
+// Each rank's symmetric buffer starts with this many bytes of flags
+// (PeerOut: entered[kMaxRanks], done[kMaxRanks]); the output follows.
+constexpr size_t kCommFlagBytes = 4096;
+static_assert(sizeof(ncclUniqueId) == QL_COMM_ID_BYTES, "unique id size");
+static_assert(QL_COMM_MAX_RANKS == ql::kMaxRanks, "rank limit");
+
+}  // namespace
+
+struct ql_comm {
+  ql_ctx* ctx = nullptr;
+  int nranks = 1;
+  int rank = 0;
+  int mode = QL_COMM_P2P;
+  ncclComm_t nccl = nullptr;
+  char* sym = nullptr;                      // this rank's [flags][output]
+  size_t out_bytes = 0;
+  char* base[ql::kMaxRanks] = {};           // every rank's symmetric buffer, mapped here
+  int32_t* arrivals = nullptr;              // CTA arrival counter of the exchange
+  uint32_t epoch = 0;                       // sharded calls made so far
+  void* stage = nullptr;                    // compact local rows of non-fused calls
+  void* gather = nullptr;                   // QL_COMM_NCCL: rank-major gathered rows
+};
+
+namespace {
+
+void release_comm(ql_comm* cm) {
+  for (int p = 0; p < cm->nranks; ++p)
+    if (p != cm->rank && cm->base[p]) cudaIpcCloseMemHandle(cm->base[p]);
+  if (cm->sym) cudaFree(cm->sym);
+  if (cm->arrivals) cudaFree(cm->arrivals);
+  if (cm->stage) cudaFree(cm->stage);
+  if (cm->gather) cudaFree(cm->gather);
+  if (cm->nccl) nccl_api().comm_destroy(cm->nccl);
+  delete cm;
+}
+
+}  // namespace
+
+int ql_comm_unique_id(ql_comm_id* out) {
+  if (!out) return fail(QL_ERR_INVALID, "ql_comm_unique_id: NULL argument");
+  const NcclApi& nc = nccl_api();
+  if (!nc.ok) return fail(QL_ERR_UNSUPPORTED, "NCCL is not available: %s", nc.why.c_str());
+  ncclUniqueId id;
+  const ncclResult_t r = nc.get_unique_id(&id);
+  if (r != ncclSuccess) return nccl_fail(r, "ncclGetUniqueId");
+  std::memcpy(out->bytes, &id, sizeof id);
+  return QL_OK;
+}
+
+int ql_comm_create(ql_ctx* c, int nranks, int rank, const ql_comm_id* id,
+                   uint64_t max_out_bytes, int mode, ql_comm** out) {
+  if (!c || !id || !out) return fail(QL_ERR_INVALID, "ql_comm_create: NULL argument");
+  if (nranks < 1 || nranks > ql::kMaxRanks)
+    return fail(QL_ERR_INVALID, "nranks %d is outside 1..%d", nranks, ql::kMaxRanks);
+  if (rank < 0 || rank >= nranks)
+    return fail(QL_ERR_INVALID, "rank %d is outside 0..%d", rank, nranks - 1);
+  if (mode != QL_COMM_P2P && mode != QL_COMM_NCCL)
+    return fail(QL_ERR_INVALID, "unknown communicator mode %d", mode);
+  if (max_out_bytes == 0) return fail(QL_ERR_INVALID, "max_out_bytes must be positive");
+  const NcclApi& nc = nccl_api();
+  if (!nc.ok) return fail(QL_ERR_UNSUPPORTED, "NCCL is not available: %s", nc.why.c_str());
+  QL_CUDA(cudaSetDevice(c->device), "set device");
+  ql_comm* cm = new ql_comm;
+  cm->ctx = c;
+  cm->nranks = nranks;
+  cm->rank = rank;
+  cm->mode = mode;
+  cm->out_bytes = align256(static_cast<size_t>(max_out_bytes));
+  auto bail = [&](int code) {
+    release_comm(cm);
+    return code;
+  };
+  ncclUniqueId uid;
+  std::memcpy(&uid, id->bytes, sizeof uid);
+  ncclResult_t nr = nc.comm_init_rank(&cm->nccl, nranks, uid, rank);
+  if (nr != ncclSuccess) {
+    cm->nccl = nullptr;
+    return bail(nccl_fail(nr, "ncclCommInitRank"));
+  }
+  cudaError_t e = cudaMalloc(&cm->sym, kCommFlagBytes + cm->out_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&cm->arrivals, 256);
+  if (e == cudaSuccess) e = cudaMalloc(&cm->stage, cm->out_bytes);
+  if (e == cudaSuccess && mode == QL_COMM_NCCL) e = cudaMalloc(&cm->gather, cm->out_bytes);
+  if (e == cudaSuccess) e = cudaMemset(cm->sym, 0, kCommFlagBytes);
+  if (e == cudaSuccess) e = cudaMemset(cm->arrivals, 0, 256);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return bail(cuda_fail(e, "allocate the communicator's buffers"));
+  cm->base[rank] = cm->sym;
+  if (nranks > 1) {
+    // One all-gather of every rank's buffer handle, size and mode: every rank
+    // must have made the same buffer (remote stores assume it) and mode.
+    struct Card {
+      cudaIpcMemHandle_t handle;
+      uint64_t out_bytes;
+      int64_t mode;
+    };
+    Card mine{};
+    mine.out_bytes = cm->out_bytes;
+    mine.mode = mode;
+    if (mode == QL_COMM_P2P) {
+      e = cudaIpcGetMemHandle(&mine.handle, cm->sym);
+      if (e != cudaSuccess) return bail(cuda_fail(e, "export the output buffer"));
+    }
+    std::vector<Card> all(nranks);
+    char* dh = nullptr;
+    e = cudaMalloc(&dh, nranks * sizeof(Card));
+    if (e == cudaSuccess)
+      e = cudaMemcpy(dh + rank * sizeof(Card), &mine, sizeof(Card), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      if (dh) cudaFree(dh);
+      return bail(cuda_fail(e, "stage the buffer cards"));
+    }
+    nr = nc.all_gather(dh + rank * sizeof(Card), dh, sizeof(Card), ncclUint8, cm->nccl,
+                       c->stream);
+    if (nr == ncclSuccess) {
+      e = cudaStreamSynchronize(c->stream);
+      if (e == cudaSuccess)
+        e = cudaMemcpy(all.data(), dh, nranks * sizeof(Card), cudaMemcpyDeviceToHost);
+    }
+    cudaFree(dh);
+    if (nr != ncclSuccess) return bail(nccl_fail(nr, "exchange the buffer cards"));
+    if (e != cudaSuccess) return bail(cuda_fail(e, "exchange the buffer cards"));
+    for (int p = 0; p < nranks; ++p)
+      if (all[p].out_bytes != cm->out_bytes || all[p].mode != mode)
+        return bail(fail(QL_ERR_INVALID, "rank %d made its communicator with %llu output bytes "
+                         "and mode %lld, rank %d with %zu and %d: every rank must pass the same",
+                         p, static_cast<unsigned long long>(all[p].out_bytes),
+                         static_cast<long long>(all[p].mode), rank, cm->out_bytes, mode));
+    for (int p = 0; p < nranks && mode == QL_COMM_P2P; ++p) {
+      if (p == rank) continue;
+      void* ptr = nullptr;
+      e = cudaIpcOpenMemHandle(&ptr, all[p].handle, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) return bail(cuda_fail(e, "map another rank's output buffer"));
+      cm->base[p] = static_cast<char*>(ptr);
+    }
+  }
+  *out = cm;
+  return QL_OK;
+}
+
+int ql_comm_destroy(ql_comm* cm) {
+  if (!cm) return fail(QL_ERR_INVALID, "ql_comm_destroy: NULL argument");
+  QL_CUDA(cudaSetDevice(cm->ctx->device), "set device");
+  QL_CUDA(cudaStreamSynchronize(cm->ctx->stream), "synchronize before destroying");
+  if (cm->nranks > 1) {
+    // No rank unmaps or frees while another may still store into it.
+    const ncclResult_t nr = nccl_api().all_gather(
+        static_cast<char*>(cm->stage) + cm->rank * 4, cm->stage, 4, ncclUint8, cm->nccl,
+        cm->ctx->stream);
+    if (nr != ncclSuccess) return nccl_fail(nr, "barrier before destroying");
+    QL_CUDA(cudaStreamSynchronize(cm->ctx->stream), "barrier before destroying");
+  }
+  release_comm(cm);
+  return QL_OK;
+}
+
+int ql_comm_buffer(ql_comm* cm, void** out, uint64_t* bytes) {
+  if (!cm || !out) return fail(QL_ERR_INVALID, "ql_comm_buffer: NULL argument");
+  *out = cm->sym + kCommFlagBytes;
+  if (bytes) *bytes = cm->out_bytes;
+  return QL_OK;
+}
+
+int ql_attn_forward_sharded(ql_ctx* c, ql_kv* kv, ql_comm* cm, const ql_attn_args* a) {
+  if (!c || !kv || !cm || !a) return fail(QL_ERR_INVALID, "ql_attn_forward_sharded: NULL argument");
+  if (cm->ctx != c)
+    return fail(QL_ERR_INVALID, "the communicator belongs to another context");
+  if (a->mem != QL_MEM_DEVICE)
+    return fail(QL_ERR_INVALID, "ql_attn_forward_sharded takes device buffers only");
+  if (!valid_io_dtype(a->out_dtype))
+    return fail(QL_ERR_INVALID, "unknown input/output dtype (%d, %d)", a->in_dtype, a->out_dtype);
+  if (a->num_heads <= 0 || a->num_kv_heads <= 0 || a->head_dim <= 0 || a->batch < 1 ||
+      a->new_len < 0)
+    return attn_forward_impl(c, kv, a, nullptr);  // the operator's own messages
+  const int nranks = cm->nranks, hq_l = a->num_heads, hd = a->head_dim;
+  const size_t eb = elem_bytes(a->out_dtype);
+  const int64_t rows = static_cast<int64_t>(a->batch) * a->new_len;
+  const size_t row_bytes = static_cast<size_t>(hq_l) * hd * eb;  // this rank's part of a row
+  if (static_cast<size_t>(rows) * row_bytes * nranks > cm->out_bytes)
+    return fail(QL_ERR_INVALID, "the output (%lld rows of %zu bytes) exceeds the communicator's "
+                "buffer of %zu bytes", static_cast<long long>(rows), row_bytes * nranks,
+                cm->out_bytes);
+  if (nranks == 1 || rows == 0) return attn_forward_impl(c, kv, a, nullptr);
+  char* symout = cm->sym + kCommFlagBytes;
+  ql::PeerOut po{};
+  po.nranks = nranks;
+  po.rank = cm->rank;
+  po.hq_total = hq_l * nranks;
+  po.head_base = cm->rank * hq_l;
+  po.epoch = cm->epoch + 1;
+  po.arrivals = cm->arrivals;
+  for (int p = 0; p < nranks; ++p) {
+    po.out[p] = cm->base[p] + kCommFlagBytes;
+    po.flags[p] = reinterpret_cast<uint32_t*>(cm->base[p]);
+  }
+  const bool fused = cm->mode == QL_COMM_P2P && a->new_len == 1 && kv->have_maps &&
+                     a->num_heads % a->num_kv_heads == 0 &&
+                     ql::splitkv_supported(hd, kv->cfg.dtype, a->num_heads / a->num_kv_heads,
+                                           kv->cfg.page_size);
+  int r;
+  if (fused) {
+    r = attn_forward_impl(c, kv, a, &po);
+    if (r != QL_OK) return r;
+    cm->epoch = po.epoch;
+  } else {
+    ql_attn_args local = *a;
+    local.out = cm->stage;
+    r = attn_forward_impl(c, kv, &local, nullptr);
+    if (r != QL_OK) return r;
+    if (cm->mode == QL_COMM_P2P) {
+      QL_CUDA(ql::launch_peer_push(cm->stage, rows, static_cast<int>(row_bytes),
+                                   static_cast<int>(hd * eb), po, c->num_sms, c->status,
+                                   c->stream),
+              "launch the output exchange");
+      cm->epoch = po.epoch;
+    } else {
+      const ncclResult_t nr = nccl_api().all_gather(cm->stage, cm->gather, rows * row_bytes,
+                                                    ncclUint8, cm->nccl, c->stream);
+      if (nr != ncclSuccess) return nccl_fail(nr, "ncclAllGather of the outputs");
+      QL_CUDA(ql::launch_rank_to_head_major(cm->gather, a->out, nranks, rows,
+                                            static_cast<int>(row_bytes), c->stream),
+              "launch the head-major permute");
+      return QL_OK;
+    }
+  }
+  if (a->out != symout)
+    QL_CUDA(cudaMemcpyAsync(a->out, symout, static_cast<size_t>(rows) * row_bytes * nranks,
+                            cudaMemcpyDeviceToDevice, c->stream),
+            "copy the gathered output");
+  return QL_OK;
+}

@@ -20,12 +20,16 @@ enum : int { kF32 = 0, kF16 = 1, kBF16 = 2, kQ8_0 = 3 };
 enum : uint32_t {
   kStatusWaitTimeout = 1u,  // an mbarrier wait ran out of iterations
   kStatusBadPage = 2u,      // a block-table entry pointed outside the pool
+  kStatusPeerTimeout = 4u,  // another GPU of a head-sharded call did not signal in time
 };
 
 // Time bound for every spin on an mbarrier, in nanoseconds of %globaltimer:
 // far above any legitimate wait (a TMA tile lands in microseconds), short
 // enough that a copy that never completes ends the kernel in about a second.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
+// Bound for waits on another GPU's flags in a head-sharded call: the ranks
+// must issue their calls within this many nanoseconds of each other.
+constexpr uint64_t kPeerWaitLimitNs = 5000000000ull;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -194,6 +198,55 @@ __device__ __forceinline__ void store_elem(void* base, size_t i, int dt, float x
   if (dt == kF32) static_cast<float*>(base)[i] = x;
   else if (dt == kF16) static_cast<__half*>(base)[i] = __float2half_rn(x);
   else static_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(x);
+}
+
+// Elements i..i+7 (i a multiple of 8) from x[0..8): one 16-byte store for
+// f16/bf16, two for f32, when `vec` says the base is 16-byte aligned; else
+// element by element.  Rounding is the same either way (to nearest even).
+__device__ __forceinline__ void store8(void* base, size_t i, int dt, const float* x, bool vec) {
+  if (!vec) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) store_elem(base, i + e, dt, x[e]);
+    return;
+  }
+  if (dt == kF32) {
+    float4* p = reinterpret_cast<float4*>(static_cast<float*>(base) + i);
+    p[0] = make_float4(x[0], x[1], x[2], x[3]);
+    p[1] = make_float4(x[4], x[5], x[6], x[7]);
+    return;
+  }
+  uint32_t w[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    w[e] = dt == kF16 ? pack2<false>(x[2 * e], x[2 * e + 1]) : pack2<true>(x[2 * e], x[2 * e + 1]);
+  *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + i) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// ------------------------------------------- flags shared between GPUs --
+// System-scope release store / acquire load, for flags that another GPU
+// writes or reads over NVLink.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait until the epoch counter *p reaches `epoch` (wrap-safe); raises
+// kStatusPeerTimeout and returns false after kPeerWaitLimitNs.
+__device__ __forceinline__ bool wait_epoch(const uint32_t* p, uint32_t epoch, uint32_t* status) {
+  if (static_cast<int32_t>(ld_acquire_sys(p) - epoch) >= 0) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    for (int i = 0; i < 16; ++i) {
+      if (static_cast<int32_t>(ld_acquire_sys(p) - epoch) >= 0) return true;
+      __nanosleep(64);
+    }
+    if (global_ns() - t0 > kPeerWaitLimitNs) break;
+  }
+  if (status) atomicOr(status, kStatusPeerTimeout);
+  return false;
 }
 
 // int8x4 in one word -> two f16x2 holding (b0,b1) and (b2,b3), exactly.

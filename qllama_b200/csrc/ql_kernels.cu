@@ -20,6 +20,7 @@
 //  gather_kernel    KvCache::get (cache.rs:185-229) into f32.
 #include <math_constants.h>
 
+#include <algorithm>
 #include <atomic>
 
 #include "ql_device.cuh"
@@ -294,7 +295,8 @@ struct SplitCfg {
   static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes +
                                   16 * kQLd * 2 + 64 * sizeof(float) + 16 +
                                   (2 * kStages + 1) * sizeof(uint64_t);
-  static_assert(4 * 8 * HD * 4 <= kStages * kStageBytes, "merge buffer must fit the stages");
+  // warp partials [4][8][HD] then the output rows [8][HD], f32
+  static_assert(5 * 8 * HD * 4 <= kStages * kStageBytes, "merge buffer must fit the stages");
   static_assert((2 * 64 * 8 + 8) * 4 <= kStages * kStageBytes, "split tables must fit the stages");
 };
 
@@ -316,6 +318,66 @@ __device__ __forceinline__ void bar_consumers() {
   asm volatile("bar.sync 1, 128;" ::: "memory");
 }
 
+// ---- head-sharded output exchange (PeerOut) ----
+// One thread, after the stream dependencies are met: every rank may now store
+// into this rank's output for this call.
+__device__ __forceinline__ void peer_enter(const PeerOut& po) {
+  for (int p = 0; p < po.nranks; ++p) st_release_sys(po.flags[p] + po.rank, po.epoch);
+}
+// Before the first store into the other ranks: have they all entered?
+__device__ __forceinline__ bool peer_wait_entered(const PeerOut& po, uint32_t* status) {
+  bool ok = true;
+  for (int p = 0; p < po.nranks && ok; ++p)
+    ok = wait_epoch(po.flags[po.rank] + p, po.epoch, status);
+  return ok;
+}
+// One thread per CTA, after the CTA's stores were fenced: counts the CTA.  The
+// last CTA of the launch tells every rank that this rank's stores are
+// visible, waits until every rank has told it the same (so the output is
+// complete when the kernel ends) and re-arms the counter.
+__device__ __forceinline__ void peer_arrive(const PeerOut& po, uint32_t* status) {
+  __threadfence_system();
+  if (atomicAdd(po.arrivals, 1) != po.total_ctas - 1) return;
+  __threadfence_system();
+  for (int p = 0; p < po.nranks; ++p) st_release_sys(po.flags[p] + kMaxRanks + po.rank, po.epoch);
+  bool ok = true;
+  for (int p = 0; p < po.nranks && ok; ++p)
+    ok = wait_epoch(po.flags[po.rank] + kMaxRanks + p, po.epoch, status);
+  atomicExch(po.arrivals, 0);
+}
+
+// The 128 consumer threads write the group's output rows res[hg][0..HD): to
+// the call's output, or, for a head-sharded call, into every rank's output
+// (after every rank has entered the call), then count the CTA.
+template <int HD>
+__device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, int job, int kvh,
+                                          int tid, int* flag) {
+  const PeerOut& po = a.peer;
+  const bool vec = a.out_vec != 0;
+  if (po.nranks == 0) {
+    for (int c = tid; c < a.group * (HD / 8); c += 128) {
+      const int hg = c / (HD / 8), d0 = (c % (HD / 8)) * 8;
+      store8(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d0,
+             a.out_dtype, res + hg * HD + d0, vec);
+    }
+    return;
+  }
+  if (tid == 0) flag[1] = peer_wait_entered(po, a.status);
+  bar_consumers();
+  if (flag[1]) {
+    for (int c = tid; c < a.group * (HD / 8); c += 128) {
+      const int hg = c / (HD / 8), d0 = (c % (HD / 8)) * 8;
+      const size_t off =
+          (static_cast<size_t>(job) * po.hq_total + po.head_base + kvh * a.group + hg) * HD + d0;
+      for (int p = 0; p < po.nranks; ++p)
+        store8(po.out[p], off, a.out_dtype, res + hg * HD + d0, vec);
+    }
+  }
+  __threadfence_system();
+  bar_consumers();
+  if (tid == 0) peer_arrive(po, a.status);
+}
+
 }  // namespace
 
 template <int HD, int DT, bool DEVROPE>
@@ -335,7 +397,13 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   const int L = qpos + 1;
   const int ntiles = (L + kTile - 1) / kTile;
   const int nsplit = (ntiles + a.tiles_per_split - 1) / a.tiles_per_split;
-  if (split >= nsplit) return;
+  if (split >= nsplit) {
+    if (a.peer.nranks) {  // still counted, once the previous call is done with the counter
+      griddep_wait();
+      if (threadIdx.x == 0) peer_arrive(a.peer, a.status);
+    }
+    return;
+  }
   const int tile0 = split * a.tiles_per_split;
   const int my_tiles = min(ntiles, tile0 + a.tiles_per_split) - tile0;
   const int hkv = a.cache.hkv;
@@ -372,6 +440,8 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   // this wait.  The next kernel may start its own set-up from here on.
   griddep_wait();
   griddep_launch_dependents();
+  if (a.peer.nranks && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+    peer_enter(a.peer);
 
   const RopeSrc rsrc{DEVROPE ? nullptr : a.rope + static_cast<size_t>(qpos) * (HD / 2),
                      static_cast<double>(qpos), static_cast<double>(a.rope_theta)};
@@ -658,6 +728,7 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   }
   bar_consumers();
   const int tid = threadIdx.x;
+  float* res = ob + 4 * 8 * HD;  // [8 heads][HD] output rows
   const size_t pslot = (static_cast<size_t>(job) * hkv + kvh) * a.max_splits;
   for (int idx = tid; idx < a.group * HD; idx += 128) {
     const int hg = idx / HD, d = idx % HD;
@@ -672,8 +743,7 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
       sum += ob[(w * 8 + hg) * HD + d];
     }
     if (nsplit == 1) {
-      store_elem(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d,
-                 a.out_dtype, sum / Lh);
+      res[hg * HD + d] = sum / Lh;
     } else {
       a.part_o[((pslot + split) * 8 + hg) * HD + d] = sum / Lh;
       if (d == 0) {
@@ -682,7 +752,11 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
       }
     }
   }
-  if (nsplit == 1) return;
+  if (nsplit == 1) {
+    bar_consumers();
+    emit_rows<HD>(a, res, job, kvh, tid, flag);
+    return;
+  }
   // ---- the last CTA of this (job, kv head) merges the splits
   __threadfence();
   bar_consumers();
@@ -691,7 +765,10 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
     flag[0] = prev == nsplit - 1;
   }
   bar_consumers();
-  if (!flag[0]) return;
+  if (!flag[0]) {
+    if (a.peer.nranks && tid == 0) peer_arrive(a.peer, a.status);
+    return;
+  }
   __threadfence();
   // Stage every split's (m, l) once, turn them into per-split weights, then
   // let each thread sum its outputs over the splits with independent loads.
@@ -722,10 +799,87 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
     float num = 0.f;
 #pragma unroll 8
     for (int s = 0; s < nsplit; ++s) num += wsm[s * 8 + hg] * __ldcg(po + static_cast<size_t>(s) * 8 * HD);
-    store_elem(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d,
-               a.out_dtype, num * dsm[hg]);
+    res[hg * HD + d] = num * dsm[hg];
   }
   if (tid == 0) a.counters[static_cast<size_t>(job) * hkv + kvh] = 0;
+  bar_consumers();
+  emit_rows<HD>(a, res, job, kvh, tid, flag);
+}
+
+// ------------------------------------------------ head-sharded exchange --
+// Copies this rank's compact output rows into every rank's symmetric output
+// (PeerOut protocol); used when the attention itself could not store there.
+__global__ void __launch_bounds__(256)
+    peer_push_kernel(const uint8_t* src, int64_t rows, int row_bytes, int head_bytes,
+                     const __grid_constant__ PeerOut po, uint32_t* status) {
+  __shared__ int go;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) peer_enter(po);
+    go = peer_wait_entered(po, status);
+  }
+  __syncthreads();
+  if (go) {
+    const int64_t row_stride = static_cast<int64_t>(po.hq_total) * head_bytes;
+    const int64_t dst0 = static_cast<int64_t>(po.head_base) * head_bytes;
+    const int64_t step = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    if (row_bytes % 16 == 0 && row_stride % 16 == 0 && dst0 % 16 == 0) {
+      const int per_row = row_bytes / 16;
+      for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+           i < rows * per_row; i += step) {
+        const int64_t r = i / per_row, c = i % per_row;
+        const uint4 v = *reinterpret_cast<const uint4*>(src + r * row_bytes + c * 16);
+        for (int p = 0; p < po.nranks; ++p)
+          *reinterpret_cast<uint4*>(static_cast<uint8_t*>(po.out[p]) + r * row_stride + dst0 +
+                                    c * 16) = v;
+      }
+    } else {
+      const int per_row = row_bytes / 4;
+      for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x;
+           i < rows * per_row; i += step) {
+        const int64_t r = i / per_row, c = i % per_row;
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(src + r * row_bytes + c * 4);
+        for (int p = 0; p < po.nranks; ++p)
+          *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(po.out[p]) + r * row_stride + dst0 +
+                                       c * 4) = v;
+      }
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) peer_arrive(po, status);
+}
+
+cudaError_t launch_peer_push(const void* src, int64_t rows, int row_bytes, int head_bytes,
+                             PeerOut po, int num_sms, uint32_t* status, cudaStream_t s) {
+  const int64_t units = rows * (row_bytes / 4);
+  const int blocks = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>((units + 255) / 256, 2LL * std::max(num_sms, 1))));
+  po.total_ctas = blocks;
+  peer_push_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint8_t*>(src), rows, row_bytes,
+                                          head_bytes, po, status);
+  return cudaGetLastError();
+}
+
+__global__ void __launch_bounds__(256)
+    rank_to_head_major_kernel(const uint32_t* src, uint32_t* dst, int nranks, int64_t rows,
+                              int row_words) {
+  const int64_t total = static_cast<int64_t>(nranks) * rows * row_words;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t c = i % row_words, r = (i / row_words) % rows, k = i / (row_words * rows);
+    dst[(r * nranks + k) * row_words + c] = src[i];
+  }
+}
+
+cudaError_t launch_rank_to_head_major(const void* src, void* dst, int nranks, int64_t rows,
+                                      int row_bytes, cudaStream_t s) {
+  const int64_t total = static_cast<int64_t>(nranks) * rows * (row_bytes / 4);
+  if (total == 0) return cudaSuccess;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 4096));
+  rank_to_head_major_kernel<<<blocks, 256, 0, s>>>(static_cast<const uint32_t*>(src),
+                                                   static_cast<uint32_t*>(dst), nranks, rows,
+                                                   row_bytes / 4);
+  return cudaGetLastError();
 }
 
 size_t splitkv_smem_bytes(int hd, int dtype) {

@@ -13,6 +13,29 @@ constexpr int kMaxBatch = 256;
 // Positions per KV tile of the split-KV kernels; pages hold a multiple of it.
 constexpr int kTile = 64;
 
+// GPUs that can share one head-sharded call.
+constexpr int kMaxRanks = 8;
+
+// Head-sharded output exchange over NVLink peer memory (no collective
+// library on this path).  Rank r computes query heads [head_base,
+// head_base + hq) of hq_total and stores them straight into every rank's
+// symmetric output [rows][hq_total][hd].  Each rank's flag block holds, per
+// source rank s, entered[s] (flags[.][s]: s passed its stream dependencies
+// for this call and may be written to) and done[s] (flags[.][kMaxRanks + s]:
+// every store of s into this rank has been made visible).  Flags are call
+// numbers (`epoch`) that only grow.
+struct PeerOut {
+  int32_t nranks;    // 0: unsharded, the output goes to the call's own buffer
+  int32_t rank;
+  int32_t hq_total;  // query heads of the whole layer (output row width / hd)
+  int32_t head_base; // first global query head of this rank
+  uint32_t epoch;
+  int32_t total_ctas;  // CTAs of the launch; the last to arrive signals done
+  int32_t* arrivals;   // this rank's CTA arrival counter, zero between calls
+  void* out[kMaxRanks];       // every rank's output region
+  uint32_t* flags[kMaxRanks]; // every rank's flag block
+};
+
 // Per-call sequence table, passed by value in the kernel parameters.
 struct SeqTable {
   int32_t seq[kMaxBatch];    // cache slot
@@ -72,6 +95,8 @@ struct AttnArgs {
   float* scratch;    // generic kernel: scores / probabilities
   double* scratch_d; // generic kernel: f64 contributions
   int32_t max_len;   // generic kernel: scratch row length
+  int32_t out_vec;   // `out` (and every peer output) is 16-byte aligned
+  PeerOut peer;      // split-KV kernel: head-sharded output exchange
   uint32_t* status;
   SeqTable seqs;
 };
@@ -120,6 +145,16 @@ cudaError_t launch_splitkv(const AttnArgs& a, const CUtensorMap* kmap, const CUt
 cudaError_t launch_splitkv_device_rope(const AttnArgs& a, const CUtensorMap* kmap,
                                        const CUtensorMap* vmap, int jobs, cudaStream_t s);
 cudaError_t launch_generic(const AttnArgs& a, cudaStream_t s);
+// Head-sharded calls that are not fused single-token decodes: copies this
+// rank's compact output rows [rows][row_bytes] into every rank's symmetric
+// output at byte offset (row * hq_total + head_base) * hd * elem, with the
+// entered/done protocol of PeerOut.  row_bytes must be a multiple of 4.
+cudaError_t launch_peer_push(const void* src, int64_t rows, int row_bytes, int head_bytes,
+                             PeerOut po, int num_sms, uint32_t* status, cudaStream_t s);
+// All-gather baseline: rank-major [nranks][rows][row_bytes] -> head-major
+// [rows][nranks * row_bytes].
+cudaError_t launch_rank_to_head_major(const void* src, void* dst, int nranks, int64_t rows,
+                                      int row_bytes, cudaStream_t s);
 cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s);
 
 // tcgen05 prefill: when it applies, rows of the rotated-q scratch it needs,

@@ -45,3 +45,25 @@ def test_context_reports_missing_device():
     with pytest.raises(qb.QllamaError) as e:
         qb.Context(0)
     assert e.value.code == qb.ERR_NO_DEVICE
+
+
+def test_comm_entry_points_validate_before_any_device_work():
+    L = qb.load()
+    cid = qb.CommId()
+    out = ctypes.c_void_p()
+    assert L.ql_comm_create(None, 2, 0, ctypes.byref(cid), 1 << 20, qb.COMM_P2P,
+                            ctypes.byref(out)) == qb.ERR_INVALID
+    assert b"NULL" in L.ql_last_error()
+    assert L.ql_comm_unique_id(None) == qb.ERR_INVALID
+    assert L.ql_comm_destroy(None) == qb.ERR_INVALID
+    assert L.ql_comm_buffer(None, None, None) == qb.ERR_INVALID
+    assert L.ql_attn_forward_sharded(None, None, None, None) == qb.ERR_INVALID
+
+
+def test_comm_unique_id_keeps_all_bytes():
+    """The id is opaque binary (NUL bytes included) and must cross the ABI whole."""
+    a, b = qb.comm_unique_id(), qb.comm_unique_id()
+    assert len(a) == len(b) == qb.COMM_ID_BYTES and a != b
+    cid = qb.CommId()
+    ctypes.memmove(ctypes.addressof(cid), a, qb.COMM_ID_BYTES)
+    assert ctypes.string_at(ctypes.addressof(cid), qb.COMM_ID_BYTES) == a
