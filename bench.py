@@ -69,7 +69,7 @@ WORKLOADS = {
                     "32768, batch 64, one layer of 80",
                layers=1, hq=64, hkv=8, hd=128, theta=500000.0, kv="q8_0", batch=64, prefill=0,
                len_lo=32768 - 16, len_hi=32768 - 16, decode=16, in_dtype="bf16",
-               out_dtype="bf16", page=64),
+               out_dtype="bf16", page=64, shard=True),
 }
 
 KV_BYTES = {"f16": 2.0, "bf16": 2.0, "f32": 4.0, "q8_0": 34.0 / 32.0}
@@ -260,11 +260,18 @@ def run_ours(args, w):
     blib = ctypes.CDLL(qb.build.BENCH_LIB)
     vp, i32 = ctypes.c_void_p, ctypes.c_int32
     blib.qlb_run_job.argtypes = [vp, vp, i32, i32, i32, i32, vp, i32, i32, i32, ctypes.c_float,
-                                 i32, i32] + [vp] * 8
+                                 i32, i32] + [vp] * 8 + [vp, i32]
     blib.qlb_run_job.restype = ctypes.c_int
 
     kind = w["kind"]
     Lyr, hq, hkv, hd, B = w["layers"], w["hq"], w["hkv"], w["hd"], w["batch"]
+    # Under torchrun the 70B-shaped decode splits its KV heads over the GPUs
+    # (strong scaling, outputs all-gathered inside the decode kernel); the
+    # other workloads run one independent replica per GPU (weak scaling).
+    shard = world > 1 and (args.shard == "heads" or (args.shard == "auto" and w.get("shard")))
+    if shard:
+        qb.shard_heads(hq, hkv, world, rank)  # raises unless the heads split evenly
+    hq_r, hkv_r = (hq // world, hkv // world) if shard else (hq, hkv)  # this rank's heads
     P, D = w["prefill"], w["decode"]
     tdt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}
     in_t, out_t = tdt[w["in_dtype"]], tdt[w["out_dtype"]]
@@ -280,18 +287,24 @@ def run_ours(args, w):
     ctx = qb.Context(local)
     stream = torch.cuda.Stream(device=dev)
     ctx.set_stream(stream.cuda_stream)
-    lens0 = seq_lengths(w, rank)  # lengths before the step's first new token
-    kv = qb.KvCache(ctx, Lyr, int(lens0.max()) + P + D, hkv, hd, w["kv"], w["page"], B)
+    lens0 = seq_lengths(w, 0 if shard else rank)  # lengths before the step's first new token
+    kv = qb.KvCache(ctx, Lyr, int(lens0.max()) + P + D, hkv_r, hd, w["kv"], w["page"], B)
+    comm = None
+    if shard:
+        uid = [qb.comm_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = qb.Comm(ctx, world, rank, uid[0], B * max(P, 1) * hq * hd * 4, "p2p")
     if kind == "decode":  # pre-fill: seeded N(0,1) rotated keys and values
         for layer in range(Lyr):
             for b in range(B):
                 L = int(lens0[b])
-                kk = torch.randn(L, hkv, hd, generator=gen, device=dev, dtype=torch.float16)
+                kk = torch.randn(L, hkv_r, hd, generator=gen, device=dev, dtype=torch.float16)
                 kv.update(layer, kk, kk.flip(0), np.arange(L), seq=b)
         torch.cuda.synchronize(dev)
 
-    pq, pk, pv = rnd(Lyr, B, P, hq, hd), rnd(Lyr, B, P, hkv, hd), rnd(Lyr, B, P, hkv, hd)
-    dq, dk, dv = rnd(D, Lyr, B, 1, hq, hd), rnd(D, Lyr, B, 1, hkv, hd), rnd(D, Lyr, B, 1, hkv, hd)
+    pq, pk, pv = rnd(Lyr, B, P, hq_r, hd), rnd(Lyr, B, P, hkv_r, hd), rnd(Lyr, B, P, hkv_r, hd)
+    dq = rnd(D, Lyr, B, 1, hq_r, hd)
+    dk, dv = rnd(D, Lyr, B, 1, hkv_r, hd), rnd(D, Lyr, B, 1, hkv_r, hd)
     pout = torch.empty(Lyr, B, P, hq * hd, device=dev, dtype=out_t)
     dout = torch.empty(D, Lyr, B, 1, hq * hd, device=dev, dtype=out_t)
     bufs = (pq, pk, pv, pout, dq, dk, dv, dout)
@@ -301,8 +314,9 @@ def run_ours(args, w):
         `steps` single-token steps from each sequence's length after the prefill."""
         st = np.ascontiguousarray(lens0 + P, dtype=np.int64)
         ptrs = [t.data_ptr() if t.numel() else None for t in bufs]
-        rc = blib.qlb_run_job(ctx._h, kv._h, Lyr, B, prefill, steps, st.ctypes.data, hq, hkv, hd,
-                              w["theta"], code[w["in_dtype"]], code[w["out_dtype"]], *ptrs)
+        rc = blib.qlb_run_job(ctx._h, kv._h, Lyr, B, prefill, steps, st.ctypes.data, hq_r, hkv_r,
+                              hd, w["theta"], code[w["in_dtype"]], code[w["out_dtype"]], *ptrs,
+                              comm._h if comm else None, hq)
         if rc != 0:
             raise qb.QllamaError(rc, qb.load().ql_last_error().decode())
 
@@ -384,12 +398,14 @@ def run_ours(args, w):
     eb, ib, ob = KV_BYTES[w["kv"]], IO_BYTES[w["in_dtype"]], IO_BYTES[w["out_dtype"]]
     dec_bytes = 0.0
     for s in range(D):
-        dec_bytes += Lyr * float(np.sum(lens0 + P + s + 1)) * hkv * hd * 2 * eb
-    dec_bytes += D * Lyr * B * ((hq + 4 * hkv) * hd * ib + hq * hd * ob)
-    pre_flops = 4.0 * B * hq * hd * P * (P + 1) / 2 * Lyr
+        dec_bytes += Lyr * float(np.sum(lens0 + P + s + 1)) * hkv_r * hd * 2 * eb
+    dec_bytes += D * Lyr * B * ((hq_r + 4 * hkv_r) * hd * ib + hq * hd * ob)
+    pre_flops = 4.0 * B * hq_r * hd * P * (P + 1) / 2 * Lyr
     tokens = B * (P + D)
+    # bytes and FLOPs add up over the ranks; with sharded heads the tokens do not
+    tok_mult = 1 if shard else world
     step_value = {"job": tokens, "prefill": pre_flops / 1e12, "decode": dec_bytes / 1e9}[kind]
-    value = world * args.steps * step_value / t_tot
+    value = (tok_mult if kind == "job" else world) * args.steps * step_value / t_tot
 
     # ---- e2e through the C ABI from pinned host memory
     host_in = [t.cpu().pin_memory() for t in (pq, pk, pv, dq, dk, dv)]
@@ -421,7 +437,7 @@ def run_ours(args, w):
         tt = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         t_e2e = tt.item()
-    e2e_value = world * e2e_reps * step_value / t_e2e
+    e2e_value = (tok_mult if kind == "job" else world) * e2e_reps * step_value / t_e2e
 
     # ---- roofline of the dominant kernel
     if kind == "prefill":
@@ -452,23 +468,28 @@ def run_ours(args, w):
             gbs = world * args.steps * dec_bytes / ph["decode"] / 1e9
             phases_out["decode"] = {"ms_per_step": 1e3 * ph["decode"] / args.steps,
                                     "kv_gbs": gbs, "frac_hbm": gbs / hbm,
-                                    "tok_s": world * args.steps * B * D / ph["decode"]}
+                                    "tok_s": tok_mult * args.steps * B * D / ph["decode"]}
         line = {
             "metric": METRIC, "value": value, "unit": w["unit"], "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_tot / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if shard else "weak",
+            "vs_baseline": None,
             "dtype": "q8_0/f16" if w["kv"] == "q8_0" else "f16", "data": "synthetic",
             "config": {"workload": args.workload, "desc": w["desc"], "layers": Lyr,
                        "num_heads": hq, "num_kv_heads": hkv, "head_dim": hd, "kv_dtype": w["kv"],
                        "batch_per_gpu": B, "prefill": P, "decode_steps": D,
                        "page_size": w["page"],
                        "l2": "flushed between steps (256 MB write outside the timed events)",
-                       "parallelism": f"{world} independent replica(s), one per GPU",
+                       "parallelism": (f"KV heads split over {world} GPUs ({hkv_r} KV / {hq_r} "
+                                       f"query heads each), outputs all-gathered over NVLink "
+                                       f"inside the decode kernel" if shard else
+                                       f"{world} independent replica(s), one per GPU"),
                        "timing": "CUDA events around CUDA-graph replays of the API's launches"},
             "roofline": roof, "phases": phases_out,
             "e2e": {"value": e2e_value, "unit": w["unit"], "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "path": "qlb_run_job -> ql_attn_forward per layer per token step (C ABI)"},
+                    "path": "qlb_run_job -> ql_attn_forward" + ("_sharded" if shard else "") +
+                            " per layer per token step (C ABI)"},
             "gpu_launches": launches * args.steps,
             "clocks": clocks,
         }
@@ -478,6 +499,8 @@ def run_ours(args, w):
                                                        "sample")}
         print(json.dumps(line), flush=True)
     del graphs
+    if comm:
+        comm.close()
     kv.close()
     ctx.close()
     if world > 1:
@@ -497,6 +520,9 @@ def main():
                     help="override the workload's batch (a smaller case of the same shapes, "
                          "e.g. for an ncu capture; the line then names the changed config)")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count")
+    ap.add_argument("--shard", choices=("auto", "heads", "replicas"), default="auto",
+                    help="with several GPUs: split the KV heads (auto: the 70B-shaped decode) "
+                         "or run independent replicas")
     args = ap.parse_args()
     w = dict(WORKLOADS[args.workload])
     for key in ("batch", "layers"):

@@ -1129,8 +1129,7 @@ struct ql_comm {
   char* sym = nullptr;                      // this rank's [flags][output]
   size_t out_bytes = 0;
   char* base[ql::kMaxRanks] = {};           // every rank's symmetric buffer, mapped here
-  int32_t* arrivals = nullptr;              // CTA arrival counter of the exchange
-  uint32_t epoch = 0;                       // sharded calls made so far
+  int32_t* arrivals = nullptr;              // device: CTA arrival counter, then the call count
   void* stage = nullptr;                    // compact local rows of non-fused calls
   void* gather = nullptr;                   // QL_COMM_NCCL: rank-major gathered rows
 };
@@ -1301,8 +1300,8 @@ int ql_attn_forward_sharded(ql_ctx* c, ql_kv* kv, ql_comm* cm, const ql_attn_arg
   po.rank = cm->rank;
   po.hq_total = hq_l * nranks;
   po.head_base = cm->rank * hq_l;
-  po.epoch = cm->epoch + 1;
   po.arrivals = cm->arrivals;
+  po.epoch = reinterpret_cast<uint32_t*>(cm->arrivals) + 16;  // its own 64-byte line
   for (int p = 0; p < nranks; ++p) {
     po.out[p] = cm->base[p] + kCommFlagBytes;
     po.flags[p] = reinterpret_cast<uint32_t*>(cm->base[p]);
@@ -1315,7 +1314,6 @@ int ql_attn_forward_sharded(ql_ctx* c, ql_kv* kv, ql_comm* cm, const ql_attn_arg
   if (fused) {
     r = attn_forward_impl(c, kv, a, &po);
     if (r != QL_OK) return r;
-    cm->epoch = po.epoch;
   } else {
     ql_attn_args local = *a;
     local.out = cm->stage;
@@ -1326,7 +1324,6 @@ int ql_attn_forward_sharded(ql_ctx* c, ql_kv* kv, ql_comm* cm, const ql_attn_arg
                                    static_cast<int>(hd * eb), po, c->num_sms, c->status,
                                    c->stream),
               "launch the output exchange");
-      cm->epoch = po.epoch;
     } else {
       const ncclResult_t nr = nccl_api().all_gather(cm->stage, cm->gather, rows * row_bytes,
                                                     ncclUint8, cm->nccl, c->stream);

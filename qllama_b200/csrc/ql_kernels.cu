@@ -321,29 +321,33 @@ __device__ __forceinline__ void bar_consumers() {
 // ---- head-sharded output exchange (PeerOut) ----
 // One thread, after the stream dependencies are met: every rank may now store
 // into this rank's output for this call.
-__device__ __forceinline__ void peer_enter(const PeerOut& po) {
-  for (int p = 0; p < po.nranks; ++p) st_release_sys(po.flags[p] + po.rank, po.epoch);
+__device__ __forceinline__ uint32_t peer_epoch(const PeerOut& po) {  // this call's number
+  return __ldcg(po.epoch) + 1u;
+}
+__device__ __forceinline__ void peer_enter(const PeerOut& po, uint32_t e) {
+  for (int p = 0; p < po.nranks; ++p) st_release_sys(po.flags[p] + po.rank, e);
 }
 // Before the first store into the other ranks: have they all entered?
-__device__ __forceinline__ bool peer_wait_entered(const PeerOut& po, uint32_t* status) {
+__device__ __forceinline__ bool peer_wait_entered(const PeerOut& po, uint32_t e,
+                                                  uint32_t* status) {
   bool ok = true;
-  for (int p = 0; p < po.nranks && ok; ++p)
-    ok = wait_epoch(po.flags[po.rank] + p, po.epoch, status);
+  for (int p = 0; p < po.nranks && ok; ++p) ok = wait_epoch(po.flags[po.rank] + p, e, status);
   return ok;
 }
 // One thread per CTA, after the CTA's stores were fenced: counts the CTA.  The
 // last CTA of the launch tells every rank that this rank's stores are
 // visible, waits until every rank has told it the same (so the output is
-// complete when the kernel ends) and re-arms the counter.
-__device__ __forceinline__ void peer_arrive(const PeerOut& po, uint32_t* status) {
+// complete when the kernel ends), re-arms the counter and records the call.
+__device__ __forceinline__ void peer_arrive(const PeerOut& po, uint32_t e, uint32_t* status) {
   __threadfence_system();
   if (atomicAdd(po.arrivals, 1) != po.total_ctas - 1) return;
   __threadfence_system();
-  for (int p = 0; p < po.nranks; ++p) st_release_sys(po.flags[p] + kMaxRanks + po.rank, po.epoch);
+  for (int p = 0; p < po.nranks; ++p) st_release_sys(po.flags[p] + kMaxRanks + po.rank, e);
   bool ok = true;
   for (int p = 0; p < po.nranks && ok; ++p)
-    ok = wait_epoch(po.flags[po.rank] + kMaxRanks + p, po.epoch, status);
+    ok = wait_epoch(po.flags[po.rank] + kMaxRanks + p, e, status);
   atomicExch(po.arrivals, 0);
+  atomicExch(po.epoch, e);
 }
 
 // The 128 consumer threads write the group's output rows res[hg][0..HD): to
@@ -351,7 +355,7 @@ __device__ __forceinline__ void peer_arrive(const PeerOut& po, uint32_t* status)
 // (after every rank has entered the call), then count the CTA.
 template <int HD>
 __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, int job, int kvh,
-                                          int tid, int* flag) {
+                                          int tid, int* flag, uint32_t e) {
   const PeerOut& po = a.peer;
   const bool vec = a.out_vec != 0;
   if (po.nranks == 0) {
@@ -362,7 +366,7 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
     }
     return;
   }
-  if (tid == 0) flag[1] = peer_wait_entered(po, a.status);
+  if (tid == 0) flag[1] = peer_wait_entered(po, e, a.status);
   bar_consumers();
   if (flag[1]) {
     for (int c = tid; c < a.group * (HD / 8); c += 128) {
@@ -375,7 +379,7 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
   }
   __threadfence_system();
   bar_consumers();
-  if (tid == 0) peer_arrive(po, a.status);
+  if (tid == 0) peer_arrive(po, e, a.status);
 }
 
 }  // namespace
@@ -398,9 +402,9 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   const int ntiles = (L + kTile - 1) / kTile;
   const int nsplit = (ntiles + a.tiles_per_split - 1) / a.tiles_per_split;
   if (split >= nsplit) {
-    if (a.peer.nranks) {  // still counted, once the previous call is done with the counter
+    if (a.peer.nranks) {  // still counted, once the previous call is done with the counters
       griddep_wait();
-      if (threadIdx.x == 0) peer_arrive(a.peer, a.status);
+      if (threadIdx.x == 0) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
     }
     return;
   }
@@ -440,8 +444,9 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   // this wait.  The next kernel may start its own set-up from here on.
   griddep_wait();
   griddep_launch_dependents();
+  const uint32_t epoch = a.peer.nranks ? peer_epoch(a.peer) : 0u;
   if (a.peer.nranks && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
-    peer_enter(a.peer);
+    peer_enter(a.peer, epoch);
 
   const RopeSrc rsrc{DEVROPE ? nullptr : a.rope + static_cast<size_t>(qpos) * (HD / 2),
                      static_cast<double>(qpos), static_cast<double>(a.rope_theta)};
@@ -754,7 +759,7 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   }
   if (nsplit == 1) {
     bar_consumers();
-    emit_rows<HD>(a, res, job, kvh, tid, flag);
+    emit_rows<HD>(a, res, job, kvh, tid, flag, epoch);
     return;
   }
   // ---- the last CTA of this (job, kv head) merges the splits
@@ -766,7 +771,7 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   }
   bar_consumers();
   if (!flag[0]) {
-    if (a.peer.nranks && tid == 0) peer_arrive(a.peer, a.status);
+    if (a.peer.nranks && tid == 0) peer_arrive(a.peer, epoch, a.status);
     return;
   }
   __threadfence();
@@ -803,7 +808,7 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   }
   if (tid == 0) a.counters[static_cast<size_t>(job) * hkv + kvh] = 0;
   bar_consumers();
-  emit_rows<HD>(a, res, job, kvh, tid, flag);
+  emit_rows<HD>(a, res, job, kvh, tid, flag, epoch);
 }
 
 // ------------------------------------------------ head-sharded exchange --
@@ -813,9 +818,10 @@ __global__ void __launch_bounds__(256)
     peer_push_kernel(const uint8_t* src, int64_t rows, int row_bytes, int head_bytes,
                      const __grid_constant__ PeerOut po, uint32_t* status) {
   __shared__ int go;
+  const uint32_t e = peer_epoch(po);
   if (threadIdx.x == 0) {
-    if (blockIdx.x == 0) peer_enter(po);
-    go = peer_wait_entered(po, status);
+    if (blockIdx.x == 0) peer_enter(po, e);
+    go = peer_wait_entered(po, e, status);
   }
   __syncthreads();
   if (go) {
@@ -846,7 +852,7 @@ __global__ void __launch_bounds__(256)
   }
   __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0) peer_arrive(po, status);
+  if (threadIdx.x == 0) peer_arrive(po, e, status);
 }
 
 cudaError_t launch_peer_push(const void* src, int64_t rows, int row_bytes, int head_bytes,

@@ -23,15 +23,17 @@ constexpr int kMaxRanks = 8;
 // source rank s, entered[s] (flags[.][s]: s passed its stream dependencies
 // for this call and may be written to) and done[s] (flags[.][kMaxRanks + s]:
 // every store of s into this rank has been made visible).  Flags are call
-// numbers (`epoch`) that only grow.
+// numbers that only grow: a launch's number is *epoch + 1, read once its
+// stream dependencies are met, and its last CTA stores it back, so a
+// captured CUDA graph replays correctly.
 struct PeerOut {
   int32_t nranks;    // 0: unsharded, the output goes to the call's own buffer
   int32_t rank;
   int32_t hq_total;  // query heads of the whole layer (output row width / hd)
   int32_t head_base; // first global query head of this rank
-  uint32_t epoch;
   int32_t total_ctas;  // CTAs of the launch; the last to arrive signals done
   int32_t* arrivals;   // this rank's CTA arrival counter, zero between calls
+  uint32_t* epoch;     // this rank's count of sharded calls (device)
   void* out[kMaxRanks];       // every rank's output region
   uint32_t* flags[kMaxRanks]; // every rank's flag block
 };
