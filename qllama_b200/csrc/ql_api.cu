@@ -329,6 +329,23 @@ SplitPlan plan_splits(const std::vector<int>& tiles, long long per_row, long lon
   return plan;
 }
 
+// Tiles per split of the wide kernel: up to kWideTilesPerGroup tiles per
+// consumer group (each group runs its tiles one after another, the groups in
+// parallel), with at most one CTA per SM over all `pairs` (token, KV head)
+// jobs; one split per job whenever that covers the sequence, so no merge
+// across CTAs is needed.
+#ifndef QL_WIDE_TILES_PER_GROUP
+#define QL_WIDE_TILES_PER_GROUP 4
+#endif
+int wide_tiles_per_split(int max_tiles, int groups, long long pairs, int num_sms) {
+  constexpr int kWideTilesPerGroup = QL_WIDE_TILES_PER_GROUP;
+  long long splits = (max_tiles + 1LL * groups * kWideTilesPerGroup - 1) /
+                     (1LL * groups * kWideTilesPerGroup);
+  splits = std::min<long long>(splits, std::max<long long>(1, num_sms / std::max(1LL, pairs)));
+  splits = std::max<long long>(1, std::min<long long>(splits, 64));
+  return static_cast<int>((max_tiles + splits - 1) / splits);
+}
+
 }  // namespace
 
 // ---------------------------------------------------- no-allocation decode --
@@ -796,7 +813,27 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
     max_tiles = std::max(max_tiles, row_tiles[b]);
   }
   int tps = max_tiles, max_splits = 1;
-  if (fast) {
+  // Too few (token, KV head) jobs to fill half the SMs: the wide kernel, whose
+  // consumer groups share each split's tiles, one CTA per SM (latency).
+  const int wide_kg = fast ? ql::splitkv_wide_groups(hd, kv->cfg.dtype) : 0;
+  const bool latency = fast && 2LL * jobs * hkv <= c->num_sms;
+  // A short context in that regime: up to kMaxCluster CTAs of about
+  // kClusterTiles tiles each per job, as one thread-block cluster that merges
+  // through distributed shared memory (each CTA streams its tiles on its own
+  // SM; one SM's TMA alone moves a few tens of GB/s).
+  constexpr int kMaxCluster = 8, kClusterTiles = 2;
+  const int cluster_ctas = (max_tiles + kClusterTiles - 1) / kClusterTiles;
+  const bool clustered = latency && max_tiles > 1 && cluster_ctas <= kMaxCluster;
+  const bool wide = !clustered && latency && wide_kg > 0;
+  int cluster = 0;
+  if (clustered) {
+    tps = (max_tiles + cluster_ctas - 1) / cluster_ctas;
+    max_splits = (max_tiles + tps - 1) / tps;
+    cluster = max_splits;
+  } else if (wide) {
+    tps = wide_tiles_per_split(max_tiles, wide_kg, 1LL * jobs * hkv, c->num_sms);
+    max_splits = (max_tiles + tps - 1) / tps;
+  } else if (fast) {
     const int per_sm = std::max(1, ql::splitkv_ctas_per_sm(hd, kv->cfg.dtype, false));
     const SplitPlan plan =
         plan_splits(row_tiles, static_cast<long long>(n) * hkv, 1LL * per_sm * c->num_sms);
@@ -915,6 +952,8 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
   at.scratch_d = reinterpret_cast<double*>(w + o_gd);
   at.max_len = max_len;
   at.out_vec = (reinterpret_cast<uintptr_t>(out) % 16) == 0;
+  at.wide = wide ? 1 : 0;
+  at.cluster = cluster;
   at.status = c->status;
   at.seqs = st;
   if (peer) {

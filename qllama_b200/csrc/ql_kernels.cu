@@ -18,6 +18,7 @@
 //                   sequential f32 P.V) so its results track the reference to
 //                   the last bit in all but rare f64-exp rounding cases.
 //  gather_kernel    KvCache::get (cache.rs:185-229) into f32.
+#include <cooperative_groups.h>
 #include <math_constants.h>
 
 #include <algorithm>
@@ -278,8 +279,15 @@ cudaError_t launch_generic(const AttnArgs& a, cudaStream_t s) {
 // ---------------------------------------------------------------- splitkv --
 namespace {
 
-template <int HD, int DT>
+template <int HD, int DT, int KG = 1>
 struct SplitCfg {
+  // KG groups of four consumer warps per CTA: KG == 1 streams one split per
+  // CTA at two or three CTAs per SM (throughput); KG > 1 (f16/bf16 only) lets
+  // the groups take alternate tiles of one split in parallel, one CTA per SM,
+  // for calls with too few (token, KV head) jobs to fill the GPU (latency).
+  static constexpr int kConsumerWarps = 4 * KG;
+  static constexpr int kConsumers = 32 * kConsumerWarps;
+  static constexpr int kThreads = kConsumers + 32;
   static constexpr bool kQ8 = DT == kQ8_0;
   static constexpr bool kBF = DT == kBF16;
   // K and V tile bytes of one 64-position stage
@@ -287,16 +295,27 @@ struct SplitCfg {
   static constexpr int kScaleBytes = kQ8 ? kTile * (HD / 32) * 2 : 0;
   static constexpr int kRaw = 2 * kKBytes + 2 * kScaleBytes;
   static constexpr int kStageBytes = (kRaw + 1023) / 1024 * 1024;
-  // Q8_0 keeps three stages so that three CTAs (15 warps) fit on an SM.
-  static constexpr int kStages = kQ8 ? 3 : (HD == 128 ? 3 : 6);
-  static constexpr int kMinCtas = kQ8 ? 3 : 2;  // resident CTAs per SM the registers allow
+  // Q8_0 keeps three stages so that three CTAs (15 warps) fit on an SM; the
+  // wide variant fills most of the SM's shared memory with stages.
+  static constexpr int kStages = KG > 1 ? 192 * 1024 / kStageBytes
+                                        : (kQ8 ? 3 : (HD == 128 ? 3 : 6));
+  static constexpr int kMinCtas = KG > 1 ? 1 : (kQ8 ? 3 : 2);  // resident CTAs per SM
   static constexpr int kTx = kRaw;
   static constexpr int kQLd = HD + 8;  // q tile row stride (elements), padded
   static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes +
-                                  16 * kQLd * 2 + 64 * sizeof(float) + 16 +
+                                  16 * kQLd * 2 + 16 * kConsumerWarps * sizeof(float) + 16 +
                                   (2 * kStages + 1) * sizeof(uint64_t);
-  // warp partials [4][8][HD] then the output rows [8][HD], f32
-  static_assert(5 * 8 * HD * 4 <= kStages * kStageBytes, "merge buffer must fit the stages");
+  // Cluster mode (KG == 1): rank 0's gather area for the other CTAs' rows
+  // [kMaxCluster][8][HD] and (max, sum) [kMaxCluster][8][2], f32, past the
+  // regular layout; only clustered launches request these bytes.
+  static constexpr int kMaxCluster = 8;
+  static constexpr size_t kGatherOff = (kSmem - 1024 + 15) / 16 * 16;
+  static constexpr size_t kGatherBytes = kMaxCluster * 8 * (HD + 2) * sizeof(float);
+  static constexpr size_t kSmemCluster = 1024 + kGatherOff + kGatherBytes;
+  // warp partials [warps][8][HD], the output rows [8][HD] and (max, sum) [8][2], f32
+  static_assert(((kConsumerWarps + 1) * 8 * HD + 16) * 4 <= kStages * kStageBytes,
+                "merge buffer must fit the stages");
+  static_assert(KG == 1 || (!kQ8 && kStages >= KG), "wide variant: f16/bf16, a stage per group");
   static_assert((2 * 64 * 8 + 8) * 4 <= kStages * kStageBytes, "split tables must fit the stages");
 };
 
@@ -314,8 +333,10 @@ __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   return static_cast<uint32_t>(row * 128 + (((chunk ^ (row & 7))) << 4));
 }
 
+// Barrier of the consumer warps only (the producer warp may have returned).
+template <int N>
 __device__ __forceinline__ void bar_consumers() {
-  asm volatile("bar.sync 1, 128;" ::: "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(N) : "memory");
 }
 
 // ---- head-sharded output exchange (PeerOut) ----
@@ -353,13 +374,13 @@ __device__ __forceinline__ void peer_arrive(const PeerOut& po, uint32_t e, uint3
 // The 128 consumer threads write the group's output rows res[hg][0..HD): to
 // the call's output, or, for a head-sharded call, into every rank's output
 // (after every rank has entered the call), then count the CTA.
-template <int HD>
+template <int HD, int NCT>
 __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, int job, int kvh,
                                           int tid, int* flag, uint32_t e) {
   const PeerOut& po = a.peer;
   const bool vec = a.out_vec != 0;
   if (po.nranks == 0) {
-    for (int c = tid; c < a.group * (HD / 8); c += 128) {
+    for (int c = tid; c < a.group * (HD / 8); c += NCT) {
       const int hg = c / (HD / 8), d0 = (c % (HD / 8)) * 8;
       store8(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d0,
              a.out_dtype, res + hg * HD + d0, vec);
@@ -367,9 +388,9 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
     return;
   }
   if (tid == 0) flag[1] = peer_wait_entered(po, e, a.status);
-  bar_consumers();
+  bar_consumers<NCT>();
   if (flag[1]) {
-    for (int c = tid; c < a.group * (HD / 8); c += 128) {
+    for (int c = tid; c < a.group * (HD / 8); c += NCT) {
       const int hg = c / (HD / 8), d0 = (c % (HD / 8)) * 8;
       const size_t off =
           (static_cast<size_t>(job) * po.hq_total + po.head_base + kvh * a.group + hg) * HD + d0;
@@ -378,17 +399,19 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
     }
   }
   __threadfence_system();
-  bar_consumers();
+  bar_consumers<NCT>();
   if (tid == 0) peer_arrive(po, e, a.status);
 }
 
 }  // namespace
 
-template <int HD, int DT, bool DEVROPE>
-__global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
+template <int HD, int DT, bool DEVROPE, int KG>
+__global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, DT, KG>::kMinCtas)
     splitkv_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, int job0) {
-  using C = SplitCfg<HD, DT>;
+  using C = SplitCfg<HD, DT, KG>;
+  constexpr int NCW = C::kConsumerWarps;  // consumer warps; warp NCW is the producer
+  constexpr int NCT = C::kConsumers;
   constexpr bool Q8 = C::kQ8;
   constexpr bool BF = C::kBF;  // bf16 operands for both MMAs; f16 otherwise
   constexpr int NKS = HD / 16;  // k-steps of QK^T
@@ -401,7 +424,22 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   const int L = qpos + 1;
   const int ntiles = (L + kTile - 1) / kTile;
   const int nsplit = (ntiles + a.tiles_per_split - 1) / a.tiles_per_split;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t* stages = smem;
+  // The CTA's merged rows [8][HD] (normalised) and their (max, sum) [8][2]:
+  // what the cluster merge reads from every CTA's shared memory.
+  float* res = reinterpret_cast<float*>(stages) + NCW * 8 * HD;
+  float* cml = res + 8 * HD;
+  // Cluster mode: the splits of one (token, KV head) form a thread-block
+  // cluster along x and merge through distributed shared memory; every CTA of
+  // the cluster reaches both cluster barriers below on every path.
+  const bool cl = a.cluster > 1;
+
   if (split >= nsplit) {
+    if (cl) cooperative_groups::this_cluster().sync();  // nothing to give rank 0
     if (a.peer.nranks) {  // still counted, once the previous call is done with the counters
       griddep_wait();
       if (threadIdx.x == 0) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
@@ -412,18 +450,16 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   const int my_tiles = min(ntiles, tile0 + a.tiles_per_split) - tile0;
   const int hkv = a.cache.hkv;
 
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint8_t* stages = smem;
   uint16_t* qs = reinterpret_cast<uint16_t*>(smem + C::kStages * C::kStageBytes);
-  float* ml = reinterpret_cast<float*>(qs + 16 * C::kQLd);
-  int* flag = reinterpret_cast<int*>(ml + 64);
+  float* ml = reinterpret_cast<float*>(qs + 16 * C::kQLd);  // [NCW][8][2] (m, l)
+  int* flag = reinterpret_cast<int*>(ml + 16 * NCW);
   uint64_t* full = reinterpret_cast<uint64_t*>(flag + 4);
   uint64_t* empty = full + C::kStages;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
+  // consumer group, and the 16-position slice of a tile the warp takes
+  const int grp = KG == 1 ? 0 : warp >> 2, slice = KG == 1 ? warp : warp & 3;
 
   uint64_t* appended = empty + C::kStages;  // the fused append is written and fenced
   const bool appends = a.fuse_append && split == nsplit - 1;
@@ -439,6 +475,12 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
     tma_prefetch_desc(&vmap);
   }
   __syncthreads();
+  // Page ids of the first 32 tiles, one per producer lane.  Only the host
+  // writes the block table (synchronously, before any launch that reads it),
+  // so they are fetched before the stream dependency is met.
+  const int* bt = a.cache.block_table + static_cast<size_t>(seq) * a.cache.pages_per_seq;
+  int lane_page = 0;
+  if (warp == NCW && lane < my_tiles) lane_page = __ldg(bt + (tile0 + lane) * kTile / a.cache.page);
   // Programmatic dependent launch: everything above overlaps the previous
   // kernel; Q/K/V and the cache may come from it, so they are read only after
   // this wait.  The next kernel may start its own set-up from here on.
@@ -454,38 +496,55 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   // ------------------------------------------------------------ producer --
   // Streams this split's tiles right away, while the consumers rotate q; only
   // the tile holding the new token waits until its K/V row has been appended.
-  if (warp == 4) {
-    if (lane == 0) {
-      const int* bt = a.cache.block_table + static_cast<size_t>(seq) * a.cache.pages_per_seq;
-      for (int i = 0; i < my_tiles; ++i) {
-        const int st = i % C::kStages;
-        if (i >= C::kStages && !mbar_wait(&empty[st], ((i / C::kStages) - 1) & 1, a.status))
-          break;
-        if (appends && i == my_tiles - 1 && !mbar_wait(appended, 0, a.status)) break;
-        const int p0 = (tile0 + i) * kTile;
-        int page = bt[p0 / a.cache.page];
-        if (page < 0 || page >= a.cache.num_pages) {
-          atomicOr(a.status, kStatusBadPage);
-          page = 0;  // keep the pipeline consistent; the result is flagged
-        }
-        const int row = (page * hkv + kvh) * a.cache.page + p0 % a.cache.page;
-        uint8_t* sb = stages + st * C::kStageBytes;
-        mbar_arrive_expect_tx(&full[st], C::kTx);
-        if constexpr (Q8) {
-          tma_load_2d(sb, &kmap, 0, row, &full[st]);
-          tma_load_2d(sb + C::kKBytes, &vmap, 0, row, &full[st]);
-          bulk_load(sb + 2 * C::kKBytes, a.cache.k_scale + static_cast<size_t>(row) * (HD / 32),
-                    C::kScaleBytes, &full[st]);
-          bulk_load(sb + 2 * C::kKBytes + C::kScaleBytes,
-                    a.cache.v_scale + static_cast<size_t>(row) * (HD / 32), C::kScaleBytes,
-                    &full[st]);
-        } else {
+  if (warp == NCW) {
+    // Tile i of the split into stage i % kStages (lane 0).
+    auto issue = [&](int i, int page) {
+      const int st = i % C::kStages;
+      const int p0 = (tile0 + i) * kTile;
+      if (page < 0 || page >= a.cache.num_pages) {
+        atomicOr(a.status, kStatusBadPage);
+        page = 0;  // keep the pipeline consistent; the result is flagged
+      }
+      const int row = (page * hkv + kvh) * a.cache.page + p0 % a.cache.page;
+      uint8_t* sb = stages + st * C::kStageBytes;
+      mbar_arrive_expect_tx(&full[st], C::kTx);
+      if constexpr (Q8) {
+        tma_load_2d(sb, &kmap, 0, row, &full[st]);
+        tma_load_2d(sb + C::kKBytes, &vmap, 0, row, &full[st]);
+        bulk_load(sb + 2 * C::kKBytes, a.cache.k_scale + static_cast<size_t>(row) * (HD / 32),
+                  C::kScaleBytes, &full[st]);
+        bulk_load(sb + 2 * C::kKBytes + C::kScaleBytes,
+                  a.cache.v_scale + static_cast<size_t>(row) * (HD / 32), C::kScaleBytes,
+                  &full[st]);
+      } else {
 #pragma unroll
-          for (int box = 0; box < HD / 64; ++box) {
-            tma_load_2d(sb + box * 8192, &kmap, box * 64, row, &full[st]);
-            tma_load_2d(sb + C::kKBytes + box * 8192, &vmap, box * 64, row, &full[st]);
-          }
+        for (int box = 0; box < HD / 64; ++box) {
+          tma_load_2d(sb + box * 8192, &kmap, box * 64, row, &full[st]);
+          tma_load_2d(sb + C::kKBytes + box * 8192, &vmap, box * 64, row, &full[st]);
         }
+      }
+    };
+    // The lanes hold the page ids of 32 tiles at a time, so no dependent
+    // global load sits between two copies; lane 0 waits for free stages (and,
+    // for the tile holding the new token, for the fused append) and issues.
+    bool alive = true;
+    for (int i0 = 0; i0 < my_tiles && alive; i0 += 32) {
+      if (i0 > 0)
+        lane_page = i0 + lane < my_tiles ? __ldg(bt + (tile0 + i0 + lane) * kTile / a.cache.page)
+                                         : 0;
+      const int n = min(32, my_tiles - i0);
+      for (int j = 0; j < n && alive; ++j) {
+        const int page = __shfl_sync(0xffffffffu, lane_page, j);
+        if (lane == 0) {
+          const int i = i0 + j, st = i % C::kStages;
+          if (i >= C::kStages && !mbar_wait(&empty[st], ((i / C::kStages) - 1) & 1, a.status))
+            alive = false;
+          else if (appends && i == my_tiles - 1 && !mbar_wait(appended, 0, a.status))
+            alive = false;
+          else
+            issue(i, page);
+        }
+        alive = __shfl_sync(0xffffffffu, alive, 0);
       }
     }
     return;
@@ -505,7 +564,7 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   }
   // Rotated query rows of this KV head's group, split hi/lo: row g holds the
   // high part of head g, row g+8 the remainder.
-  for (int idx = threadIdx.x; idx < 8 * (HD / 2); idx += 128) {
+  for (int idx = threadIdx.x; idx < 8 * (HD / 2); idx += NCT) {
     const int hg = idx / (HD / 2), p = idx % (HD / 2);
     float y0 = 0.f, y1 = 0.f;
     if (hg < a.group) {
@@ -524,7 +583,7 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
     qs[(hg + 8) * C::kQLd + k0] = static_cast<uint16_t>(ll & 0xffff);
     qs[(hg + 8) * C::kQLd + k1] = static_cast<uint16_t>(ll >> 16);
   }
-  bar_consumers();
+  bar_consumers<NCT>();
 
   // ----------------------------------------------------------- consumers --
   // A fragments of q: k-step ks starts 32 bytes after k-step ks-1.  The f16
@@ -545,12 +604,12 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   float m = -CUDART_INF_F, l = 0.f;
   const float sl2 = a.scale * kLog2e;
 
-  for (int i = 0; i < my_tiles; ++i) {
+  for (int i = grp; i < my_tiles; i += KG) {  // the group's tiles of this split
     const int st = i % C::kStages;
     const bool ok = mbar_wait(&full[st], (i / C::kStages) & 1, a.status);
     if (__any_sync(0xffffffffu, !ok)) break;
     uint8_t* sb = stages + st * C::kStageBytes;
-    const int valid = L - (tile0 + i) * kTile - 16 * warp;  // live positions in my 16-row slice
+    const int valid = L - (tile0 + i) * kTile - 16 * slice;  // live positions in my slice
     if (valid > 0) {
       if (valid < 16) {
         // Rows past the sequence end hold stale data; zero their V so that
@@ -558,10 +617,10 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
         if constexpr (Q8) {
           uint16_t* vsc = reinterpret_cast<uint16_t*>(sb + 2 * C::kKBytes + C::kScaleBytes);
           for (int r = valid + lane / (HD / 32); r < 16; r += 32 / (HD / 32))
-            vsc[(16 * warp + r) * (HD / 32) + lane % (HD / 32)] = 0;
+            vsc[(16 * slice + r) * (HD / 32) + lane % (HD / 32)] = 0;
         } else {
           for (int idx = lane; idx < (16 - valid) * (HD / 8); idx += 32) {
-            const int r = 16 * warp + valid + idx / (HD / 8), c = idx % (HD / 8);
+            const int r = 16 * slice + valid + idx / (HD / 8), c = idx % (HD / 8);
             *reinterpret_cast<uint4*>(sb + C::kKBytes + (c >> 3) * 8192 + swz128(r, c & 7)) =
                 make_uint4(0, 0, 0, 0);
           }
@@ -581,7 +640,7 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
             ldmatrix_x4(qaddr + (2 * blk + s2) * 32, qf[0], qf[1], qf[2], qf[3]);
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
-              const int r = 16 * warp + 8 * nt + g;
+              const int r = 16 * slice + 8 * nt + g;
               const int byte = 32 * blk + 16 * s2 + 4 * tq;
               const uint32_t w =
                   *reinterpret_cast<const uint32_t*>(sb + swz128(r, byte >> 4) + (byte & 15));
@@ -592,7 +651,7 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
           }
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
-            const int r0 = 16 * warp + 8 * nt + 2 * tq;
+            const int r0 = 16 * slice + 8 * nt + 2 * tq;
             const float d0 = __half2float(__ushort_as_half(ksc[r0 * (HD / 32) + blk]));
             const float d1 = __half2float(__ushort_as_half(ksc[(r0 + 1) * (HD / 32) + blk]));
             s[nt][0] += d0 * sb2[nt][0];
@@ -605,7 +664,7 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
         const uint32_t kbase = smem_u32(sb);
 #pragma unroll
         for (int ks = 0; ks < NKS; ++ks) {
-          const int r = 16 * warp + (lane >> 4) * 8 + (lane & 7);
+          const int r = 16 * slice + (lane >> 4) * 8 + (lane & 7);
           const int c = 2 * ks + ((lane >> 3) & 1);
           uint32_t b0, b1, b2, b3;
           ldmatrix_x4(kbase + (c >> 3) * 8192 + swz128(r, c & 7), b0, b1, b2, b3);
@@ -658,7 +717,7 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
         const uint8_t* vq = sb + C::kKBytes;
         const uint16_t* vsc =
             reinterpret_cast<const uint16_t*>(sb + 2 * C::kKBytes + C::kScaleBytes);
-        const int rA = 16 * warp + 2 * tq;
+        const int rA = 16 * slice + 2 * tq;
         const uint4 A = *reinterpret_cast<const uint4*>(vq + swz128(rA, g));
         const uint4 B = *reinterpret_cast<const uint4*>(vq + swz128(rA + 1, g));
         const uint4 Cq = *reinterpret_cast<const uint4*>(vq + swz128(rA + 8, g));
@@ -695,7 +754,7 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
         const uint32_t vbase = smem_u32(sb + C::kKBytes);
 #pragma unroll
         for (int jj = 0; jj < HD / 16; ++jj) {
-          const int r = 16 * warp + ((lane >> 3) & 1) * 8 + (lane & 7);
+          const int r = 16 * slice + ((lane >> 3) & 1) * 8 + (lane & 7);
           const int c = 2 * jj + (lane >> 4);
           uint32_t b0, b1, b2, b3;
           ldmatrix_x4_trans(vbase + (c >> 3) * 8192 + swz128(r, c & 7), b0, b1, b2, b3);
@@ -711,18 +770,18 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   // ------------------------------------------------------------- epilogue --
   l += __shfl_xor_sync(0xffffffffu, l, 1);
   l += __shfl_xor_sync(0xffffffffu, l, 2);
-  bar_consumers();  // every consumer is done reading the stages
+  bar_consumers<NCT>();  // every consumer is done reading the stages
   if (tq == 0) {
     ml[(warp * 8 + g) * 2] = m;
     ml[(warp * 8 + g) * 2 + 1] = l;
   }
-  bar_consumers();
+  bar_consumers<NCT>();
   float M = -CUDART_INF_F;
 #pragma unroll
-  for (int w = 0; w < 4; ++w) M = fmaxf(M, ml[(w * 8 + g) * 2]);
+  for (int w = 0; w < NCW; ++w) M = fmaxf(M, ml[(w * 8 + g) * 2]);
   const float Mb = M == -CUDART_INF_F ? 0.f : M;
   const float f = exp2f(m - Mb);
-  float* ob = reinterpret_cast<float*>(stages);  // [4 warps][8 heads][HD]
+  float* ob = reinterpret_cast<float*>(stages);  // [NCW warps][8 heads][HD]
 #pragma unroll
   for (int j = 0; j < NO; ++j) {
     // Q8_0 columns were permuted: n-tile j, column n -> head-dim 16n + j.
@@ -731,24 +790,27 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
     ob[(warp * 8 + g) * HD + c0] = (o[j][0] + o[j][2]) * f;
     ob[(warp * 8 + g) * HD + c1] = (o[j][1] + o[j][3]) * f;
   }
-  bar_consumers();
+  bar_consumers<NCT>();
   const int tid = threadIdx.x;
-  float* res = ob + 4 * 8 * HD;  // [8 heads][HD] output rows
   const size_t pslot = (static_cast<size_t>(job) * hkv + kvh) * a.max_splits;
-  for (int idx = tid; idx < a.group * HD; idx += 128) {
+  for (int idx = tid; idx < a.group * HD; idx += NCT) {
     const int hg = idx / HD, d = idx % HD;
     float Mh = -CUDART_INF_F;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) Mh = fmaxf(Mh, ml[(w * 8 + hg) * 2]);
+    for (int w = 0; w < NCW; ++w) Mh = fmaxf(Mh, ml[(w * 8 + hg) * 2]);
     const float Mhb = Mh == -CUDART_INF_F ? 0.f : Mh;
     float Lh = 0.f, sum = 0.f;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) {
+    for (int w = 0; w < NCW; ++w) {
       Lh += ml[(w * 8 + hg) * 2 + 1] * exp2f(ml[(w * 8 + hg) * 2] - Mhb);
       sum += ob[(w * 8 + hg) * HD + d];
     }
-    if (nsplit == 1) {
+    if (nsplit == 1 || cl) {
       res[hg * HD + d] = sum / Lh;
+      if (d == 0) {
+        cml[2 * hg] = Mh;
+        cml[2 * hg + 1] = Lh;
+      }
     } else {
       a.part_o[((pslot + split) * 8 + hg) * HD + d] = sum / Lh;
       if (d == 0) {
@@ -757,19 +819,55 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
       }
     }
   }
+  if (cl) {
+    namespace cgr = cooperative_groups;
+    cgr::cluster_group cluster = cgr::this_cluster();
+    float* grows = reinterpret_cast<float*>(smem + C::kGatherOff);  // [rank][8][HD]
+    float* gml = grows + C::kMaxCluster * 8 * HD;                    // [rank][8][2]
+    bar_consumers<NCT>();  // res and cml are complete
+    if (split != 0) {  // push this split's rows and (max, sum) into rank 0's shared memory
+      float* drow = cluster.map_shared_rank(grows, 0) + split * 8 * HD;
+      float* dml = cluster.map_shared_rank(gml, 0) + split * 16;
+      for (int i = tid; i < a.group * HD / 4; i += NCT)
+        reinterpret_cast<float4*>(drow)[i] = reinterpret_cast<const float4*>(res)[i];
+      if (tid < 16) dml[tid] = cml[tid];
+    }
+    cluster.sync();  // the pushes are visible to rank 0; the others may exit
+    if (split == 0) {  // rank 0 merges the live splits' rows by LSE weight
+      for (int idx = tid; idx < a.group * HD; idx += NCT) {
+        const int hg = idx / HD, d = idx % HD;
+        float Mx = cml[2 * hg];
+        for (int r = 1; r < nsplit; ++r) Mx = fmaxf(Mx, gml[r * 16 + 2 * hg]);
+        const float Mxb = Mx == -CUDART_INF_F ? 0.f : Mx;
+        float den = cml[2 * hg + 1] * exp2f(cml[2 * hg] - Mxb);
+        float num = den * res[hg * HD + d];
+        for (int r = 1; r < nsplit; ++r) {
+          const float w = gml[r * 16 + 2 * hg + 1] * exp2f(gml[r * 16 + 2 * hg] - Mxb);
+          num += w * grows[(r * 8 + hg) * HD + d];
+          den += w;
+        }
+        res[hg * HD + d] = num / den;
+      }
+      bar_consumers<NCT>();
+      emit_rows<HD, NCT>(a, res, job, kvh, tid, flag, epoch);
+    } else if (a.peer.nranks && tid == 0) {
+      peer_arrive(a.peer, epoch, a.status);
+    }
+    return;
+  }
   if (nsplit == 1) {
-    bar_consumers();
-    emit_rows<HD>(a, res, job, kvh, tid, flag, epoch);
+    bar_consumers<NCT>();
+    emit_rows<HD, NCT>(a, res, job, kvh, tid, flag, epoch);
     return;
   }
   // ---- the last CTA of this (job, kv head) merges the splits
   __threadfence();
-  bar_consumers();
+  bar_consumers<NCT>();
   if (tid == 0) {
     const int prev = atomicAdd(&a.counters[static_cast<size_t>(job) * hkv + kvh], 1);
     flag[0] = prev == nsplit - 1;
   }
-  bar_consumers();
+  bar_consumers<NCT>();
   if (!flag[0]) {
     if (a.peer.nranks && tid == 0) peer_arrive(a.peer, epoch, a.status);
     return;
@@ -780,11 +878,11 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
   float* wsm = reinterpret_cast<float*>(stages);  // [split][8] weights
   float* msm = wsm + 64 * 8;                      // [split][8] maxima
   float* dsm = msm + 64 * 8;                      // [8] 1 / sum of weights
-  for (int i = tid; i < nsplit * 8; i += 128) {
+  for (int i = tid; i < nsplit * 8; i += NCT) {
     msm[i] = __ldcg(&a.part_ml[((pslot + (i >> 3)) * 8 + (i & 7)) * 2]);
     wsm[i] = __ldcg(&a.part_ml[((pslot + (i >> 3)) * 8 + (i & 7)) * 2 + 1]);
   }
-  bar_consumers();
+  bar_consumers<NCT>();
   if (tid < 8) {
     float Mx = -CUDART_INF_F;
     for (int s = 0; s < nsplit; ++s) Mx = fmaxf(Mx, msm[s * 8 + tid]);
@@ -797,8 +895,8 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
     }
     dsm[tid] = 1.f / den;
   }
-  bar_consumers();
-  for (int idx = tid; idx < a.group * HD; idx += 128) {
+  bar_consumers<NCT>();
+  for (int idx = tid; idx < a.group * HD; idx += NCT) {
     const int hg = idx / HD, d = idx % HD;
     const float* po = a.part_o + (pslot * 8 + hg) * HD + d;
     float num = 0.f;
@@ -807,8 +905,8 @@ __global__ void __launch_bounds__(160, SplitCfg<HD, DT>::kMinCtas)
     res[hg * HD + d] = num * dsm[hg];
   }
   if (tid == 0) a.counters[static_cast<size_t>(job) * hkv + kvh] = 0;
-  bar_consumers();
-  emit_rows<HD>(a, res, job, kvh, tid, flag, epoch);
+  bar_consumers<NCT>();
+  emit_rows<HD, NCT>(a, res, job, kvh, tid, flag, epoch);
 }
 
 // ------------------------------------------------ head-sharded exchange --
@@ -888,7 +986,7 @@ cudaError_t launch_rank_to_head_major(const void* src, void* dst, int nranks, in
   return cudaGetLastError();
 }
 
-size_t splitkv_smem_bytes(int hd, int dtype) {
+size_t splitkv_smem_bytes(int hd, int dtype) {  // the KG == 1 variant
   if (dtype == kQ8_0) return SplitCfg<128, kQ8_0>::kSmem;
   if (hd == 128) return dtype == kBF16 ? SplitCfg<128, kBF16>::kSmem : SplitCfg<128, kF16>::kSmem;
   return dtype == kBF16 ? SplitCfg<64, kBF16>::kSmem : SplitCfg<64, kF16>::kSmem;
@@ -902,9 +1000,9 @@ bool splitkv_supported(int hd, int dtype, int group, int page) {
 
 // Sets the kernel's shared-memory limit on the current device (once per
 // device) and reports how many of its CTAs an SM holds.
-template <int HD, int DT, bool DEVROPE>
+template <int HD, int DT, bool DEVROPE, int KG>
 static cudaError_t configure_splitkv_t(int* ctas_per_sm) {
-  using C = SplitCfg<HD, DT>;
+  using C = SplitCfg<HD, DT, KG>;
   constexpr int kMaxDev = 64;
   static std::atomic<int> occupancy[kMaxDev];  // 0 = not configured yet
   int dev = 0;
@@ -914,12 +1012,13 @@ static cudaError_t configure_splitkv_t(int* ctas_per_sm) {
     if (ctas_per_sm) *ctas_per_sm = occupancy[dev].load(std::memory_order_relaxed);
     return cudaSuccess;
   }
-  e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmem));
+  e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE, KG>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(KG == 1 ? C::kSmemCluster : C::kSmem));
   if (e != cudaSuccess) return e;
   int n = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, splitkv_kernel<HD, DT, DEVROPE>, 160,
-                                                    C::kSmem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, splitkv_kernel<HD, DT, DEVROPE, KG>,
+                                                    C::kThreads, C::kSmem);
   if (e != cudaSuccess) return e;
   n = max(n, 1);
   if (dev < kMaxDev) occupancy[dev].store(n, std::memory_order_release);
@@ -927,39 +1026,65 @@ static cudaError_t configure_splitkv_t(int* ctas_per_sm) {
   return cudaSuccess;
 }
 
-template <int HD, int DT, bool DEVROPE>
+template <int HD, int DT, bool DEVROPE, int KG>
 static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
                                     const CUtensorMap* vmap, int jobs, cudaStream_t s, bool pdl) {
-  using C = SplitCfg<HD, DT>;
-  cudaError_t e = configure_splitkv_t<HD, DT, DEVROPE>(nullptr);
+  using C = SplitCfg<HD, DT, KG>;
+  cudaError_t e = configure_splitkv_t<HD, DT, DEVROPE, KG>(nullptr);
   if (e != cudaSuccess) return e;
   for (int j0 = 0; j0 < jobs; j0 += 65535) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.max_splits, a.cache.hkv, min(65535, jobs - j0));
-    cfg.blockDim = dim3(160);
-    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.blockDim = dim3(C::kThreads);
+    cfg.dynamicSmemBytes = a.cluster > 1 ? C::kSmemCluster : C::kSmem;
     cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+      attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[na].val.programmaticStreamSerializationAllowed = 1;
+      ++na;
+    }
+    if (a.cluster > 1) {  // the splits of one job as one cluster (grid x == cluster size)
+      attr[na].id = cudaLaunchAttributeClusterDimension;
+      attr[na].val.clusterDim.x = a.cluster;
+      attr[na].val.clusterDim.y = 1;
+      attr[na].val.clusterDim.z = 1;
+      ++na;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    e = cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE>, a, *kmap, *vmap, j0);
+    cfg.numAttrs = na;
+    e = cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG>, a, *kmap, *vmap, j0);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
+}
+
+// Consumer groups of the wide (latency) variant for a configuration, 0 if it
+// has none: four at head_dim 64, two at 128 (the register file bounds it).
+constexpr int wide_groups(int hd, int dt) {
+  return dt == kQ8_0 ? 0 : (hd == 64 ? 4 : (hd == 128 ? 2 : 0));
 }
 
 template <bool DEVROPE>
 static cudaError_t dispatch_splitkv(const AttnArgs& a, const CUtensorMap* kmap,
                                     const CUtensorMap* vmap, int jobs, cudaStream_t s, bool pdl) {
   const int hd = a.cache.hd, dt = a.cache.dtype;
-  if (dt == kQ8_0) return launch_splitkv_t<128, kQ8_0, DEVROPE>(a, kmap, vmap, jobs, s, pdl);
+  if constexpr (!DEVROPE) {
+    if (a.wide && wide_groups(hd, dt)) {
+      if (hd == 128)
+        return dt == kBF16 ? launch_splitkv_t<128, kBF16, false, 2>(a, kmap, vmap, jobs, s, pdl)
+                           : launch_splitkv_t<128, kF16, false, 2>(a, kmap, vmap, jobs, s, pdl);
+      return dt == kBF16 ? launch_splitkv_t<64, kBF16, false, 4>(a, kmap, vmap, jobs, s, pdl)
+                         : launch_splitkv_t<64, kF16, false, 4>(a, kmap, vmap, jobs, s, pdl);
+    }
+  }
+  if (dt == kQ8_0) return launch_splitkv_t<128, kQ8_0, DEVROPE, 1>(a, kmap, vmap, jobs, s, pdl);
   if (hd == 128)
-    return dt == kBF16 ? launch_splitkv_t<128, kBF16, DEVROPE>(a, kmap, vmap, jobs, s, pdl)
-                       : launch_splitkv_t<128, kF16, DEVROPE>(a, kmap, vmap, jobs, s, pdl);
-  return dt == kBF16 ? launch_splitkv_t<64, kBF16, DEVROPE>(a, kmap, vmap, jobs, s, pdl)
-                     : launch_splitkv_t<64, kF16, DEVROPE>(a, kmap, vmap, jobs, s, pdl);
+    return dt == kBF16 ? launch_splitkv_t<128, kBF16, DEVROPE, 1>(a, kmap, vmap, jobs, s, pdl)
+                       : launch_splitkv_t<128, kF16, DEVROPE, 1>(a, kmap, vmap, jobs, s, pdl);
+  return dt == kBF16 ? launch_splitkv_t<64, kBF16, DEVROPE, 1>(a, kmap, vmap, jobs, s, pdl)
+                     : launch_splitkv_t<64, kF16, DEVROPE, 1>(a, kmap, vmap, jobs, s, pdl);
 }
 
 template <bool DEVROPE>
@@ -967,15 +1092,17 @@ static int ctas_per_sm_t(int hd, int dt) {
   int n = 0;
   cudaError_t e;
   if (dt == kQ8_0)
-    e = configure_splitkv_t<128, kQ8_0, DEVROPE>(&n);
+    e = configure_splitkv_t<128, kQ8_0, DEVROPE, 1>(&n);
   else if (hd == 128)
-    e = dt == kBF16 ? configure_splitkv_t<128, kBF16, DEVROPE>(&n)
-                    : configure_splitkv_t<128, kF16, DEVROPE>(&n);
+    e = dt == kBF16 ? configure_splitkv_t<128, kBF16, DEVROPE, 1>(&n)
+                    : configure_splitkv_t<128, kF16, DEVROPE, 1>(&n);
   else
-    e = dt == kBF16 ? configure_splitkv_t<64, kBF16, DEVROPE>(&n)
-                    : configure_splitkv_t<64, kF16, DEVROPE>(&n);
+    e = dt == kBF16 ? configure_splitkv_t<64, kBF16, DEVROPE, 1>(&n)
+                    : configure_splitkv_t<64, kF16, DEVROPE, 1>(&n);
   return e == cudaSuccess ? n : 0;
 }
+
+int splitkv_wide_groups(int hd, int dtype) { return wide_groups(hd, dtype); }
 
 int splitkv_ctas_per_sm(int hd, int dtype, bool device_rope) {
   return device_rope ? ctas_per_sm_t<true>(hd, dtype) : ctas_per_sm_t<false>(hd, dtype);

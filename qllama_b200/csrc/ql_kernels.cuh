@@ -98,6 +98,8 @@ struct AttnArgs {
   double* scratch_d; // generic kernel: f64 contributions
   int32_t max_len;   // generic kernel: scratch row length
   int32_t out_vec;   // `out` (and every peer output) is 16-byte aligned
+  int32_t wide;      // split-KV kernel: the variant whose consumer groups share a split
+  int32_t cluster;   // split-KV kernel: CTAs per cluster along the splits (0/1: none)
   PeerOut peer;      // split-KV kernel: head-sharded output exchange
   uint32_t* status;
   SeqTable seqs;
@@ -138,6 +140,9 @@ bool splitkv_supported(int hd, int dtype, int group, int page);
 // Resident CTAs per SM of the split-KV kernel for a configuration on the
 // current device (0 if the query failed); configures the kernel as well.
 int splitkv_ctas_per_sm(int hd, int dtype, bool device_rope);
+// Consumer groups of the split-KV kernel's wide variant (one CTA per SM, the
+// groups take alternate tiles of a split), 0 when the configuration has none.
+int splitkv_wide_groups(int hd, int dtype);
 
 cudaError_t launch_append(const AppendArgs& a, cudaStream_t s);
 cudaError_t launch_splitkv(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,

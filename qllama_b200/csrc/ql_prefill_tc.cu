@@ -264,30 +264,46 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
         for (int hf = 0; hf < C::kHalves; ++hf)
           tma_load_2d(qsm + q * C::kQBytes + hf * (kBM * 128), &qmap, hf * 64, qrow, q_full);
       }
-      const int* bt = a.cache.block_table + static_cast<size_t>(seq) * a.cache.pages_per_seq;
-      const int oob_row = a.cache.num_pages * hkv * a.cache.page;  // past the pool: zero fill
-      for (int j = 0; j < n_kv; ++j) {
-        const int st = j & 1;
-        if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, a.status)) break;
-        uint8_t* ks = stg + st * C::kStageBytes;
-        uint8_t* vs = ks + C::kKBytes;
-        mbar_arrive_expect_tx(&kv_full[st], C::kStageBytes);
+    }
+    // Page rows of 32 sub-tiles (64 keys each) at a time, one per lane, so no
+    // dependent global load sits between two copies; lane 0 issues the K/V
+    // tiles of 128 keys as stages free up.
+    const int* bt = a.cache.block_table + static_cast<size_t>(seq) * a.cache.pages_per_seq;
+    const int oob_row = a.cache.num_pages * hkv * a.cache.page;  // past the pool: zero fill
+    bool alive = true;
+    for (int c0 = 0; c0 < 2 * n_kv && alive; c0 += 32) {
+      const int u = c0 + lane, key0 = u * 64;
+      int lane_row = oob_row;
+      if (u < 2 * n_kv && key0 / a.cache.page < a.cache.pages_per_seq) {
+        const int page = __ldg(bt + key0 / a.cache.page);
+        if (page >= 0 && page < a.cache.num_pages)
+          lane_row = (page * hkv + kvh) * a.cache.page + key0 % a.cache.page;
+      }
+      const int n = min(32, 2 * n_kv - c0);
+      for (int jj = 0; jj < n && alive; jj += 2) {
+        const int rows[2] = {__shfl_sync(0xffffffffu, lane_row, jj),
+                             __shfl_sync(0xffffffffu, lane_row, jj + 1)};
+        if (lane == 0) {
+          const int j = (c0 + jj) / 2, st = j & 1;
+          if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, a.status)) {
+            alive = false;
+          } else {
+            uint8_t* ks = stg + st * C::kStageBytes;
+            uint8_t* vs = ks + C::kKBytes;
+            mbar_arrive_expect_tx(&kv_full[st], C::kStageBytes);
 #pragma unroll
-        for (int sub = 0; sub < 2; ++sub) {
-          const int key0 = j * kBN + sub * 64;
-          const int lp = key0 / a.cache.page;
-          int row = oob_row;
-          if (lp < a.cache.pages_per_seq) {
-            const int page = bt[lp];
-            if (page >= 0 && page < a.cache.num_pages)
-              row = (page * hkv + kvh) * a.cache.page + key0 % a.cache.page;
-          }
+            for (int sub = 0; sub < 2; ++sub) {
 #pragma unroll
-          for (int hf = 0; hf < C::kHalves; ++hf) {
-            tma_load_2d(ks + hf * (kBN * 128) + sub * 8192, &kmap, hf * 64, row, &kv_full[st]);
-            tma_load_2d(vs + hf * (kBN * 128) + sub * 8192, &vmap, hf * 64, row, &kv_full[st]);
+              for (int hf = 0; hf < C::kHalves; ++hf) {
+                tma_load_2d(ks + hf * (kBN * 128) + sub * 8192, &kmap, hf * 64, rows[sub],
+                            &kv_full[st]);
+                tma_load_2d(vs + hf * (kBN * 128) + sub * 8192, &vmap, hf * 64, rows[sub],
+                            &kv_full[st]);
+              }
+            }
           }
         }
+        alive = __shfl_sync(0xffffffffu, alive, 0);
       }
     }
   } else if (warp == 1) {
