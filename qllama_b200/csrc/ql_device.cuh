@@ -86,6 +86,49 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
   return false;
 }
 
+// ------------------------------------------------- thread-block clusters --
+// Split arrive/wait of the hardware cluster barrier (every thread of every CTA
+// arrives once, right after its mbarriers are initialised; waiting later
+// costs nothing), a remote arrive on another CTA's mbarrier with release at
+// cluster scope, and a bounded wait that acquires at cluster scope.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, uint32_t cta_rank) {
+  asm volatile(
+      "{\n\t.reg .b32 ra;\n\t"
+      "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
+      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_u32(bar)),
+      "r"(cta_rank)
+      : "memory");
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
+                                                  uint32_t* status) {
+  auto try_wait = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_wait()) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    for (int i = 0; i < 32; ++i)
+      if (try_wait()) return true;
+    if (global_ns() - t0 > kWaitLimitNs) break;
+  }
+  if (status) atomicOr(status, kStatusWaitTimeout);
+  return false;
+}
+
 // ------------------------------------------- programmatic dependent launch --
 // Waits until the grids this one depends on have completed and their memory
 // is visible (a no-op when the launch carried no programmatic dependency).

@@ -68,10 +68,12 @@ __device__ __forceinline__ double2 rope_cs(const RopeSrc& r, int p, int hd) {
 
 // One warp writes one cache row (one position of one KV head): K rotated
 // when a rotation source is given, V as is, both converted to the cache type.
+// With `stage`, the same bytes also go to shared memory as
+// [K row][V row][K scales][V scales] (the scales for Q8_0 only).
 template <bool DEV>
 __device__ void append_row_t(const void* kin, const void* vin, int in_dt, size_t in_off,
                              const RopeSrc& rope, bool rotate, const CacheView& c, int64_t dst,
-                             int lane) {
+                             int lane, uint8_t* stage = nullptr) {
   const int hd = c.hd;
   const int pairs = hd / 2;
   for (int base = 0; base < pairs; base += 32) {
@@ -99,12 +101,27 @@ __device__ void append_row_t(const void* kin, const void* vin, int in_dt, size_t
           c.k_scale[si] = __half_as_ushort(sk);
           c.v_scale[si] = __half_as_ushort(sv);
         }
+        if (stage) {
+          *reinterpret_cast<char2*>(stage + 2 * p) = make_char2(qk0, qk1);
+          *reinterpret_cast<char2*>(stage + hd + 2 * p) = make_char2(qv0, qv1);
+          if ((lane & 15) == 0) {
+            uint16_t* ss = reinterpret_cast<uint16_t*>(stage + 2 * hd);
+            ss[(2 * p) / 32] = __half_as_ushort(sk);
+            ss[hd / 32 + (2 * p) / 32] = __half_as_ushort(sv);
+          }
+        }
       }
     } else if (valid) {
       store_elem(c.k, e, c.dtype, k0);
       store_elem(c.k, e + 1, c.dtype, k1);
       store_elem(c.v, e, c.dtype, v0);
       store_elem(c.v, e + 1, c.dtype, v1);
+      if (stage && c.dtype != kF32) {
+        const uint32_t kk = c.dtype == kF16 ? pack2<false>(k0, k1) : pack2<true>(k0, k1);
+        const uint32_t vv = c.dtype == kF16 ? pack2<false>(v0, v1) : pack2<true>(v0, v1);
+        reinterpret_cast<uint32_t*>(stage)[p] = kk;
+        reinterpret_cast<uint32_t*>(stage + 2 * hd)[p] = vv;
+      }
     }
   }
 }
@@ -302,18 +319,25 @@ struct SplitCfg {
   static constexpr int kMinCtas = KG > 1 ? 1 : (kQ8 ? 3 : 2);  // resident CTAs per SM
   static constexpr int kTx = kRaw;
   static constexpr int kQLd = HD + 8;  // q tile row stride (elements), padded
-  static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes +
-                                  16 * kQLd * 2 + 16 * kConsumerWarps * sizeof(float) + 16 +
-                                  (2 * kStages + 1) * sizeof(uint64_t);
+  // the new token's converted K/V row (fused append), 16-byte aligned
+  static constexpr int kRowOff = ((16 * kQLd * 2 + 16 * kConsumerWarps * 4 + 16 +
+                                   (2 * kStages + 1) * 8) + 15) / 16 * 16;
+  static constexpr int kRowBytes = kQ8 ? 2 * HD + 2 * (HD / 32) * 2 : 4 * HD;
+  static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes + kRowOff +
+                                  (kRowBytes + 15) / 16 * 16;
   // Cluster mode (KG == 1): rank 0's gather area for the other CTAs' rows
   // [kMaxCluster][8][HD] and (max, sum) [kMaxCluster][8][2], f32, past the
   // regular layout; only clustered launches request these bytes.
   static constexpr int kMaxCluster = 8;
   static constexpr size_t kGatherOff = (kSmem - 1024 + 15) / 16 * 16;
-  static constexpr size_t kGatherBytes = kMaxCluster * 8 * (HD + 2) * sizeof(float);
+  // rows [rank][8][HD], (max, sum) [rank][16], weights [rank][8], then rank
+  // 0's arrival mbarrier
+  static constexpr size_t kGatherBytes = (kMaxCluster * 8 * HD + kMaxCluster * 24) * 4 + 16;
   static constexpr size_t kSmemCluster = 1024 + kGatherOff + kGatherBytes;
-  // warp partials [warps][8][HD], the output rows [8][HD] and (max, sum) [8][2], f32
-  static_assert(((kConsumerWarps + 1) * 8 * HD + 16) * 4 <= kStages * kStageBytes,
+  // warp partials [warps][8][HD], the output rows [8][HD], (max, sum) [8][2] and
+  // the per-(warp, head) weights [warps][8], f32
+  static_assert(((kConsumerWarps + 1) * 8 * HD + 16 + 8 * kConsumerWarps) * 4 <=
+                    kStages * kStageBytes,
                 "merge buffer must fit the stages");
   static_assert(KG == 1 || (!kQ8 && kStages >= KG), "wide variant: f16/bf16, a stage per group");
   static_assert((2 * 64 * 8 + 8) * 4 <= kStages * kStageBytes, "split tables must fit the stages");
@@ -437,9 +461,19 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   // cluster along x and merge through distributed shared memory; every CTA of
   // the cluster reaches both cluster barriers below on every path.
   const bool cl = a.cluster > 1;
+  float* grows = reinterpret_cast<float*>(smem + C::kGatherOff);  // rank 0: [rank][8][HD]
+  float* gml = grows + C::kMaxCluster * 8 * HD;                    // [rank][16] (max, sum)
+  float* gw = gml + C::kMaxCluster * 16;                           // [rank][8] weights
+  uint64_t* gbar = reinterpret_cast<uint64_t*>(gw + C::kMaxCluster * 8);  // the others arrive
 
   if (split >= nsplit) {
-    if (cl) cooperative_groups::this_cluster().sync();  // nothing to give rank 0
+    if (cl) {  // nothing to give rank 0 but the arrival it counts
+      cluster_arrive_relaxed();
+      if (threadIdx.x == 0) {
+        cluster_wait();  // rank 0's mbarrier is initialised
+        mbar_arrive_remote(gbar, 0);
+      }
+    }
     if (a.peer.nranks) {  // still counted, once the previous call is done with the counters
       griddep_wait();
       if (threadIdx.x == 0) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
@@ -462,6 +496,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   const int grp = KG == 1 ? 0 : warp >> 2, slice = KG == 1 ? warp : warp & 3;
 
   uint64_t* appended = empty + C::kStages;  // the fused append is written and fenced
+  uint8_t* newrow = reinterpret_cast<uint8_t*>(qs) + C::kRowOff;  // its converted K/V row
   const bool appends = a.fuse_append && split == nsplit - 1;
 
   if (threadIdx.x == 0) {
@@ -470,11 +505,13 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
       mbar_init(&empty[s], 4);
     }
     mbar_init(appended, 1);
+    if (cl && split == 0) mbar_init(gbar, a.cluster - 1);
     fence_mbar_init();
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
   }
   __syncthreads();
+  if (cl) cluster_arrive_relaxed();  // after the init fence: the others may now arrive on gbar
   // Page ids of the first 32 tiles, one per producer lane.  Only the host
   // writes the block table (synchronously, before any launch that reads it),
   // so they are fetched before the stream dependency is met.
@@ -525,8 +562,9 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
       }
     };
     // The lanes hold the page ids of 32 tiles at a time, so no dependent
-    // global load sits between two copies; lane 0 waits for free stages (and,
-    // for the tile holding the new token, for the fused append) and issues.
+    // global load sits between two copies; lane 0 waits for free stages and
+    // issues.  The tile holding the new token is copied at once too: its new
+    // row is patched in shared memory by the consumers.
     bool alive = true;
     for (int i0 = 0; i0 < my_tiles && alive; i0 += 32) {
       if (i0 > 0)
@@ -538,8 +576,6 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
         if (lane == 0) {
           const int i = i0 + j, st = i % C::kStages;
           if (i >= C::kStages && !mbar_wait(&empty[st], ((i / C::kStages) - 1) & 1, a.status))
-            alive = false;
-          else if (appends && i == my_tiles - 1 && !mbar_wait(appended, 0, a.status))
             alive = false;
           else
             issue(i, page);
@@ -557,7 +593,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     const int64_t dst = cache_row(a.cache, seq, qpos, kvh, a.status, ok);
     if (ok)
       append_row_t<DEVROPE>(a.k, a.v, a.in_dtype, (static_cast<size_t>(job) * hkv + kvh) * HD,
-                            rsrc, true, a.cache, dst, lane);
+                            rsrc, true, a.cache, dst, lane, newrow);
     fence_proxy_async_global();
     __syncwarp();
     if (lane == 0) mbar_arrive(appended);
@@ -623,6 +659,34 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
             const int r = 16 * slice + valid + idx / (HD / 8), c = idx % (HD / 8);
             *reinterpret_cast<uint4*>(sb + C::kKBytes + (c >> 3) * 8192 + swz128(r, c & 7)) =
                 make_uint4(0, 0, 0, 0);
+          }
+        }
+        __syncwarp();
+      }
+      if (appends && i == my_tiles - 1 && (qpos - (tile0 + i) * kTile) / 16 == slice) {
+        // This slice holds the new token: its row in the tile may be older
+        // than the append, so it is copied in from the fused append's
+        // shared-memory row (the same bytes the cache now holds).
+        const int rt = qpos - (tile0 + i) * kTile;
+        if (mbar_wait(appended, 0, a.status)) {
+          if constexpr (Q8) {
+            if (lane < 8) {
+              *reinterpret_cast<uint4*>(sb + swz128(rt, lane)) =
+                  reinterpret_cast<const uint4*>(newrow)[lane];
+              *reinterpret_cast<uint4*>(sb + C::kKBytes + swz128(rt, lane)) =
+                  reinterpret_cast<const uint4*>(newrow + HD)[lane];
+            } else if (lane < 8 + HD / 32) {
+              const int j = lane - 8;
+              const uint16_t* ss = reinterpret_cast<const uint16_t*>(newrow + 2 * HD);
+              reinterpret_cast<uint16_t*>(sb + 2 * C::kKBytes)[rt * (HD / 32) + j] = ss[j];
+              reinterpret_cast<uint16_t*>(sb + 2 * C::kKBytes + C::kScaleBytes)[rt * (HD / 32) + j] =
+                  ss[HD / 32 + j];
+            }
+          } else if (lane < HD / 8) {  // 16-byte chunk `lane`: box lane/8, chunk lane%8
+            const uint32_t off = (lane >> 3) * 8192 + swz128(rt, lane & 7);
+            *reinterpret_cast<uint4*>(sb + off) = reinterpret_cast<const uint4*>(newrow)[lane];
+            *reinterpret_cast<uint4*>(sb + C::kKBytes + off) =
+                reinterpret_cast<const uint4*>(newrow + 2 * HD)[lane];
           }
         }
         __syncwarp();
@@ -768,91 +832,127 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   }
 
   // ------------------------------------------------------------- epilogue --
+  // Each warp leaves its (max, sum) per head and its raw O rows; weights
+  // exp2(m_w - M) / L per (warp, head) are formed once; each output row is
+  // then a weighted sum over the warps, four columns per thread.
   l += __shfl_xor_sync(0xffffffffu, l, 1);
   l += __shfl_xor_sync(0xffffffffu, l, 2);
   bar_consumers<NCT>();  // every consumer is done reading the stages
+  float* ob = reinterpret_cast<float*>(stages);  // [NCW warps][8 heads][HD]
   if (tq == 0) {
     ml[(warp * 8 + g) * 2] = m;
     ml[(warp * 8 + g) * 2 + 1] = l;
   }
-  bar_consumers<NCT>();
-  float M = -CUDART_INF_F;
-#pragma unroll
-  for (int w = 0; w < NCW; ++w) M = fmaxf(M, ml[(w * 8 + g) * 2]);
-  const float Mb = M == -CUDART_INF_F ? 0.f : M;
-  const float f = exp2f(m - Mb);
-  float* ob = reinterpret_cast<float*>(stages);  // [NCW warps][8 heads][HD]
 #pragma unroll
   for (int j = 0; j < NO; ++j) {
     // Q8_0 columns were permuted: n-tile j, column n -> head-dim 16n + j.
     const int c0 = Q8 ? 16 * (2 * tq) + j : 8 * j + 2 * tq;
     const int c1 = Q8 ? 16 * (2 * tq + 1) + j : 8 * j + 2 * tq + 1;
-    ob[(warp * 8 + g) * HD + c0] = (o[j][0] + o[j][2]) * f;
-    ob[(warp * 8 + g) * HD + c1] = (o[j][1] + o[j][3]) * f;
+    ob[(warp * 8 + g) * HD + c0] = o[j][0] + o[j][2];
+    ob[(warp * 8 + g) * HD + c1] = o[j][1] + o[j][3];
   }
   bar_consumers<NCT>();
   const int tid = threadIdx.x;
-  const size_t pslot = (static_cast<size_t>(job) * hkv + kvh) * a.max_splits;
-  for (int idx = tid; idx < a.group * HD; idx += NCT) {
-    const int hg = idx / HD, d = idx % HD;
-    float Mh = -CUDART_INF_F;
+  float* wt = cml + 16;  // [NCW][8]
+  if (tid < 8) {
+    float M = -CUDART_INF_F;
 #pragma unroll
-    for (int w = 0; w < NCW; ++w) Mh = fmaxf(Mh, ml[(w * 8 + hg) * 2]);
-    const float Mhb = Mh == -CUDART_INF_F ? 0.f : Mh;
-    float Lh = 0.f, sum = 0.f;
+    for (int w = 0; w < NCW; ++w) M = fmaxf(M, ml[(w * 8 + tid) * 2]);
+    const float Mb = M == -CUDART_INF_F ? 0.f : M;
+    float Lh = 0.f;
+    for (int w = 0; w < NCW; ++w) {
+      const float e = exp2f(ml[(w * 8 + tid) * 2] - Mb);
+      wt[w * 8 + tid] = e;
+      Lh += ml[(w * 8 + tid) * 2 + 1] * e;
+    }
+    const float inv = Lh > 0.f ? 1.f / Lh : 0.f;
+    for (int w = 0; w < NCW; ++w) wt[w * 8 + tid] *= inv;
+    cml[2 * tid] = M;
+    cml[2 * tid + 1] = Lh;
+  }
+  bar_consumers<NCT>();
+  const size_t pslot = (static_cast<size_t>(job) * hkv + kvh) * a.max_splits;
+  for (int c = tid; c < a.group * (HD / 4); c += NCT) {
+    const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int w = 0; w < NCW; ++w) {
-      Lh += ml[(w * 8 + hg) * 2 + 1] * exp2f(ml[(w * 8 + hg) * 2] - Mhb);
-      sum += ob[(w * 8 + hg) * HD + d];
+      const float4 v = *reinterpret_cast<const float4*>(ob + (w * 8 + hg) * HD + d0);
+      const float ww = wt[w * 8 + hg];
+      acc.x += v.x * ww;
+      acc.y += v.y * ww;
+      acc.z += v.z * ww;
+      acc.w += v.w * ww;
     }
     if (nsplit == 1 || cl) {
-      res[hg * HD + d] = sum / Lh;
-      if (d == 0) {
-        cml[2 * hg] = Mh;
-        cml[2 * hg + 1] = Lh;
-      }
+      *reinterpret_cast<float4*>(res + hg * HD + d0) = acc;
     } else {
-      a.part_o[((pslot + split) * 8 + hg) * HD + d] = sum / Lh;
-      if (d == 0) {
-        a.part_ml[((pslot + split) * 8 + hg) * 2] = Mh;
-        a.part_ml[((pslot + split) * 8 + hg) * 2 + 1] = Lh;
+      *reinterpret_cast<float4*>(a.part_o + ((pslot + split) * 8 + hg) * HD + d0) = acc;
+      if (d0 == 0) {
+        a.part_ml[((pslot + split) * 8 + hg) * 2] = cml[2 * hg];
+        a.part_ml[((pslot + split) * 8 + hg) * 2 + 1] = cml[2 * hg + 1];
       }
     }
   }
   if (cl) {
-    namespace cgr = cooperative_groups;
-    cgr::cluster_group cluster = cgr::this_cluster();
-    float* grows = reinterpret_cast<float*>(smem + C::kGatherOff);  // [rank][8][HD]
-    float* gml = grows + C::kMaxCluster * 8 * HD;                    // [rank][8][2]
-    bar_consumers<NCT>();  // res and cml are complete
-    if (split != 0) {  // push this split's rows and (max, sum) into rank 0's shared memory
+    bar_consumers<NCT>();  // res is complete
+    if (split != 0) {
+      // Push this split's rows and (max, sum) into rank 0's shared memory,
+      // then count on rank 0's mbarrier; nothing reads this CTA afterwards.
+      namespace cgr = cooperative_groups;
+      cgr::cluster_group cluster = cgr::this_cluster();
       float* drow = cluster.map_shared_rank(grows, 0) + split * 8 * HD;
       float* dml = cluster.map_shared_rank(gml, 0) + split * 16;
       for (int i = tid; i < a.group * HD / 4; i += NCT)
         reinterpret_cast<float4*>(drow)[i] = reinterpret_cast<const float4*>(res)[i];
       if (tid < 16) dml[tid] = cml[tid];
-    }
-    cluster.sync();  // the pushes are visible to rank 0; the others may exit
-    if (split == 0) {  // rank 0 merges the live splits' rows by LSE weight
-      for (int idx = tid; idx < a.group * HD; idx += NCT) {
-        const int hg = idx / HD, d = idx % HD;
-        float Mx = cml[2 * hg];
-        for (int r = 1; r < nsplit; ++r) Mx = fmaxf(Mx, gml[r * 16 + 2 * hg]);
-        const float Mxb = Mx == -CUDART_INF_F ? 0.f : Mx;
-        float den = cml[2 * hg + 1] * exp2f(cml[2 * hg] - Mxb);
-        float num = den * res[hg * HD + d];
-        for (int r = 1; r < nsplit; ++r) {
-          const float w = gml[r * 16 + 2 * hg + 1] * exp2f(gml[r * 16 + 2 * hg] - Mxb);
-          num += w * grows[(r * 8 + hg) * HD + d];
-          den += w;
-        }
-        res[hg * HD + d] = num / den;
+      bar_consumers<NCT>();  // every push is issued before the release below
+      if (tid == 0) {
+        cluster_wait();  // rank 0's mbarrier is initialised
+        mbar_arrive_remote(gbar, 0);
+        if (a.peer.nranks) peer_arrive(a.peer, epoch, a.status);
       }
-      bar_consumers<NCT>();
-      emit_rows<HD, NCT>(a, res, job, kvh, tid, flag, epoch);
-    } else if (a.peer.nranks && tid == 0) {
-      peer_arrive(a.peer, epoch, a.status);
+      return;
     }
+    // Rank 0: every other CTA has pushed (bounded wait, acquire at cluster
+    // scope); merge the live splits by LSE weight.
+    mbar_wait_cluster(gbar, 0, a.status);
+    if (tid < a.group) {
+      float M = cml[2 * tid];
+      for (int r = 1; r < nsplit; ++r) M = fmaxf(M, gml[r * 16 + 2 * tid]);
+      const float Mb = M == -CUDART_INF_F ? 0.f : M;
+      float den = 0.f;
+      for (int r = 0; r < nsplit; ++r) {
+        const float mr = r == 0 ? cml[2 * tid] : gml[r * 16 + 2 * tid];
+        const float lr = r == 0 ? cml[2 * tid + 1] : gml[r * 16 + 2 * tid + 1];
+        const float w = lr * exp2f(mr - Mb);
+        gw[r * 8 + tid] = w;
+        den += w;
+      }
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      for (int r = 0; r < nsplit; ++r) gw[r * 8 + tid] *= inv;
+    }
+    bar_consumers<NCT>();
+    for (int c = tid; c < a.group * (HD / 4); c += NCT) {
+      const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
+      float4 acc = *reinterpret_cast<const float4*>(res + hg * HD + d0);
+      const float w0 = gw[hg];
+      acc.x *= w0;
+      acc.y *= w0;
+      acc.z *= w0;
+      acc.w *= w0;
+      for (int r = 1; r < nsplit; ++r) {
+        const float4 v = *reinterpret_cast<const float4*>(grows + (r * 8 + hg) * HD + d0);
+        const float ww = gw[r * 8 + hg];
+        acc.x += v.x * ww;
+        acc.y += v.y * ww;
+        acc.z += v.z * ww;
+        acc.w += v.w * ww;
+      }
+      *reinterpret_cast<float4*>(res + hg * HD + d0) = acc;
+    }
+    bar_consumers<NCT>();
+    emit_rows<HD, NCT>(a, res, job, kvh, tid, flag, epoch);
     return;
   }
   if (nsplit == 1) {
