@@ -821,7 +821,14 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
   // kClusterTiles tiles each per job, as one thread-block cluster that merges
   // through distributed shared memory (each CTA streams its tiles on its own
   // SM; one SM's TMA alone moves a few tens of GB/s).
-  constexpr int kMaxCluster = 8, kClusterTiles = 2;
+#ifndef QL_CLUSTER_TILES
+#define QL_CLUSTER_TILES 2
+#endif
+#ifndef QL_MAX_CLUSTER
+#define QL_MAX_CLUSTER 8
+#endif
+  constexpr int kMaxCluster = QL_MAX_CLUSTER, kClusterTiles = QL_CLUSTER_TILES;
+  static_assert(kMaxCluster <= 8, "the kernel's gather area holds 8 CTAs");
   const int cluster_ctas = (max_tiles + kClusterTiles - 1) / kClusterTiles;
   const bool clustered = latency && max_tiles > 1 && cluster_ctas <= kMaxCluster;
   const bool wide = !clustered && latency && wide_kg > 0;

@@ -328,7 +328,7 @@ struct SplitCfg {
   // Cluster mode (KG == 1): rank 0's gather area for the other CTAs' rows
   // [kMaxCluster][8][HD] and (max, sum) [kMaxCluster][8][2], f32, past the
   // regular layout; only clustered launches request these bytes.
-  static constexpr int kMaxCluster = 8;
+  static constexpr int kMaxCluster = 8;  // portable cluster size
   static constexpr size_t kGatherOff = (kSmem - 1024 + 15) / 16 * 16;
   // rows [rank][8][HD], (max, sum) [rank][16], weights [rank][8], then rank
   // 0's arrival mbarrier
