@@ -400,7 +400,7 @@ __device__ __forceinline__ void peer_arrive(const PeerOut& po, uint32_t e, uint3
 // (after every rank has entered the call), then count the CTA.
 template <int HD, int NCT>
 __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, int job, int kvh,
-                                          int tid, int* flag, uint32_t e) {
+                                          int tid, int* flag) {
   const PeerOut& po = a.peer;
   const bool vec = a.out_vec != 0;
   if (po.nranks == 0) {
@@ -411,6 +411,7 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
     }
     return;
   }
+  const uint32_t e = peer_epoch(po);
   if (tid == 0) flag[1] = peer_wait_entered(po, e, a.status);
   bar_consumers<NCT>();
   if (flag[1]) {
@@ -523,9 +524,11 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   // this wait.  The next kernel may start its own set-up from here on.
   griddep_wait();
   griddep_launch_dependents();
-  const uint32_t epoch = a.peer.nranks ? peer_epoch(a.peer) : 0u;
+  // A sharded call's number (*epoch + 1) is read where it is used rather than
+  // kept live through the tile loop: no CTA stores the new count before every
+  // CTA of the launch has arrived, and each CTA reads it before arriving.
   if (a.peer.nranks && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
-    peer_enter(a.peer, epoch);
+    peer_enter(a.peer, peer_epoch(a.peer));
 
   const RopeSrc rsrc{DEVROPE ? nullptr : a.rope + static_cast<size_t>(qpos) * (HD / 2),
                      static_cast<double>(qpos), static_cast<double>(a.rope_theta)};
@@ -910,7 +913,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
       if (tid == 0) {
         cluster_wait();  // rank 0's mbarrier is initialised
         mbar_arrive_remote(gbar, 0);
-        if (a.peer.nranks) peer_arrive(a.peer, epoch, a.status);
+        if (a.peer.nranks) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
       }
       return;
     }
@@ -952,12 +955,12 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
       *reinterpret_cast<float4*>(res + hg * HD + d0) = acc;
     }
     bar_consumers<NCT>();
-    emit_rows<HD, NCT>(a, res, job, kvh, tid, flag, epoch);
+    emit_rows<HD, NCT>(a, res, job, kvh, tid, flag);
     return;
   }
   if (nsplit == 1) {
     bar_consumers<NCT>();
-    emit_rows<HD, NCT>(a, res, job, kvh, tid, flag, epoch);
+    emit_rows<HD, NCT>(a, res, job, kvh, tid, flag);
     return;
   }
   // ---- the last CTA of this (job, kv head) merges the splits
@@ -969,7 +972,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   }
   bar_consumers<NCT>();
   if (!flag[0]) {
-    if (a.peer.nranks && tid == 0) peer_arrive(a.peer, epoch, a.status);
+    if (a.peer.nranks && tid == 0) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
     return;
   }
   __threadfence();
@@ -1006,7 +1009,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   }
   if (tid == 0) a.counters[static_cast<size_t>(job) * hkv + kvh] = 0;
   bar_consumers<NCT>();
-  emit_rows<HD, NCT>(a, res, job, kvh, tid, flag, epoch);
+  emit_rows<HD, NCT>(a, res, job, kvh, tid, flag);
 }
 
 // ------------------------------------------------ head-sharded exchange --
