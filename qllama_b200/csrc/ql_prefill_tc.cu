@@ -10,8 +10,9 @@
 // Warp roles:
 //   warp 0      TMA producer: the rotated Q tiles once, then K/V tiles of 128
 //               keys (two 64-position page boxes x two 64-column halves each)
-//               into a two-stage ring; boxes of unallocated pages are read out
-//               of range, which TMA fills with zeros.
+//               into a two-stage ring with separate K and V barriers; boxes of
+//               unallocated pages are read out of range, which TMA fills with
+//               zeros.
 //   warp 1      owns TMEM (512 columns) and issues every tcgen05.mma from one
 //               thread: S_q(j) = Q_q K_j^T (A and B from shared memory) and
 //               O_q += P_q(j) V_j with P taken from TMEM; completion is
@@ -27,6 +28,8 @@
 // Operands are f16 (cache f16, q rotated in f32 then rounded to f16); the
 // accumulators are f32 in TMEM.  No cluster multicast is used anywhere.
 #include <math_constants.h>
+
+#include <atomic>
 
 #include "ql_device.cuh"
 #include "ql_kernels.cuh"
@@ -216,8 +219,13 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
   uint8_t* stg = smem + C::kStageOff;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::kBarOff);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
+  // K and V of a tile have their own barriers: K is free once the tile's
+  // last S MMA is done, V only after its last PV, so K's refill starts about
+  // an iteration earlier than a shared K/V stage would allow.
+  uint64_t* k_full = bars + 11;   // [2]
+  uint64_t* k_empty = bars + 13;  // [2]
+  uint64_t* v_full = bars + 15;   // [2]
+  uint64_t* v_empty = bars + 17;  // [2]
   uint64_t* s_full = bars + 5;    // [NQ] S_q(j) computed (and everything issued before it)
   uint64_t* p_full = bars + 7;    // [NQ] P_q(j) written, O_q rescaled if needed
   uint64_t* o_done = bars + 9;    // all MMAs complete
@@ -228,8 +236,10 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     for (int q = 0; q < NQ; ++q) {
       mbar_init(&s_full[q], 1);
@@ -285,22 +295,29 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
                              __shfl_sync(0xffffffffu, lane_row, jj + 1)};
         if (lane == 0) {
           const int j = (c0 + jj) / 2, st = j & 1;
-          if (j >= 2 && !mbar_wait(&kv_empty[st], ((j >> 1) - 1) & 1, a.status)) {
+          uint8_t* ks = stg + st * C::kStageBytes;
+          uint8_t* vs = ks + C::kKBytes;
+          if (j >= 2 && !mbar_wait(&k_empty[st], ((j >> 1) - 1) & 1, a.status)) {
             alive = false;
           } else {
-            uint8_t* ks = stg + st * C::kStageBytes;
-            uint8_t* vs = ks + C::kKBytes;
-            mbar_arrive_expect_tx(&kv_full[st], C::kStageBytes);
+            mbar_arrive_expect_tx(&k_full[st], C::kKBytes);
 #pragma unroll
-            for (int sub = 0; sub < 2; ++sub) {
+            for (int sub = 0; sub < 2; ++sub)
 #pragma unroll
-              for (int hf = 0; hf < C::kHalves; ++hf) {
+              for (int hf = 0; hf < C::kHalves; ++hf)
                 tma_load_2d(ks + hf * (kBN * 128) + sub * 8192, &kmap, hf * 64, rows[sub],
-                            &kv_full[st]);
+                            &k_full[st]);
+          }
+          if (alive && j >= 2 && !mbar_wait(&v_empty[st], ((j >> 1) - 1) & 1, a.status)) {
+            alive = false;
+          } else if (alive) {
+            mbar_arrive_expect_tx(&v_full[st], C::kKBytes);
+#pragma unroll
+            for (int sub = 0; sub < 2; ++sub)
+#pragma unroll
+              for (int hf = 0; hf < C::kHalves; ++hf)
                 tma_load_2d(vs + hf * (kBN * 128) + sub * 8192, &vmap, hf * 64, rows[sub],
-                            &kv_full[st]);
-              }
-            }
+                            &v_full[st]);
           }
         }
         alive = __shfl_sync(0xffffffffu, alive, 0);
@@ -335,7 +352,8 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
                     smem_desc(vaddr + ks * 2048, kBN * 128, 1024), idesc_o, (j > 0 || ks > 0));
       };
       for (int j = 0; ok && j < n_kv; ++j) {
-        ok = mbar_wait(&kv_full[j & 1], (j >> 1) & 1, a.status);
+        ok = mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.status);
+        if (ok && j > 0) ok = mbar_wait(&v_full[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status);
         if (!ok) break;
         for (int q = 0; q < NQ; ++q) {
           if (j > 0) {  // P_q(j-1) is in S_q's columns: consume it before S_q(j) overwrites them
@@ -345,12 +363,14 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
             }
             tc_fence_after();
             issue_pv(q, j - 1);
-            if (q == NQ - 1) tc_commit(&kv_empty[(j - 1) & 1]);
+            if (q == NQ - 1) tc_commit(&v_empty[(j - 1) & 1]);
           }
           tc_fence_after();
           issue_s(q, j);
         }
+        if (ok) tc_commit(&k_empty[j & 1]);  // every S of tile j reads K(j) only
       }
+      if (ok) ok = mbar_wait(&v_full[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, a.status);
       for (int q = 0; ok && q < NQ; ++q) {
         if (!mbar_wait(&p_full[q], (n_kv - 1) & 1, a.status)) break;
         tc_fence_after();
@@ -381,11 +401,12 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
       }
       tc_fence_after();
       const int key0 = j * kBN;
-      if (q == 0 && j == n_kv - 1 && key0 + r >= kv_end) {
+      if (q == 0 && j == n_kv - 1 && key0 + r >= kv_end &&
+          mbar_wait(&v_full[j & 1], (j >> 1) & 1, a.status)) {
         // Key r of the last tile lies past the sequence end: its V row may be
         // stale pool memory (Inf/NaN), and P = 0 times Inf would still reach
-        // O.  Zero it before the PV MMAs read it (V landed before S_0 was
-        // issued; every PV of this tile is issued after P_0 is released).
+        // O.  Zero it once V has landed and before the PV MMAs read it (every
+        // PV of this tile is issued after P_0 is released).
         uint8_t* vrow = stg + (j & 1) * C::kStageBytes + C::kKBytes + r * 128;
 #pragma unroll
         for (int hf = 0; hf < C::kHalves; ++hf)
@@ -544,13 +565,17 @@ static cudaError_t launch_prefill_nq(const PrefillArgs& a, const CUtensorMap* qm
                                      const CUtensorMap* kmap, const CUtensorMap* vmap,
                                      cudaStream_t s) {
   using C = PrefillCfg<128, NQ>;
-  static bool configured = false;
-  if (!configured) {
-    cudaError_t e = cudaFuncSetAttribute(prefill_tc_kernel<128, NQ>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(C::kSmem));
+  constexpr int kMaxDev = 64;
+  static std::atomic<bool> configured[kMaxDev];  // shared-memory limit set on that device
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev >= kMaxDev || !configured[dev].load(std::memory_order_acquire)) {
+    e = cudaFuncSetAttribute(prefill_tc_kernel<128, NQ>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(C::kSmem));
     if (e != cudaSuccess) return e;
-    configured = true;
+    if (dev < kMaxDev) configured[dev].store(true, std::memory_order_release);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.new_len + kBM - 1) / kBM, a.hq / NQ, a.batch);
