@@ -205,6 +205,18 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
   }
 }
 
+// D(16x8,s32) += A(16x32, row) * B(32x8, col), A/B signed 8-bit.  Register
+// a0 holds A[g][4t..4t+3], a1 A[g+8][4t..], a2 A[g][16+4t..], a3
+// A[g+8][16+4t..]; b0 holds B[4t..4t+3][g], b1 B[16+4t..][g]; d as for
+// mma16816 (g = lane / 4, t = lane % 4).
+__device__ __forceinline__ void mma16832_s8(int (&d)[4], const uint4& a, uint32_t b0,
+                                            uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
+}
+
 // -------------------------------------------------------------- elements --
 template <bool BF>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {

@@ -341,15 +341,22 @@ struct SplitCfg {
                 "merge buffer must fit the stages");
   static_assert(KG == 1 || (!kQ8 && kStages >= KG), "wide variant: f16/bf16, a stage per group");
   static_assert((2 * 64 * 8 + 8) * 4 <= kStages * kStageBytes, "split tables must fit the stages");
+  // Q8_0 int8 q fragments [HD/32][32][4 words], per-head factors [8] and
+  // half-row maxima [8][HD/64] in the q tile's space
+  static_assert(!kQ8 || (HD / 32) * 512 + (8 + 8 * (HD / 64)) * 4 <= 16 * kQLd * 2,
+                "Q8_0 q fragments must fit the q tile");
 };
 
-// Logical MMA k index of physical head-dim element d for int8 K rows: a
-// thread's four values of one k-step sit in 4 consecutive bytes, so one
-// 32-bit shared load feeds its B fragment, and each 16-wide k-step stays
-// inside one 32-element Q8_0 block.
-__device__ __forceinline__ int q8_logical_k(int d) {
-  const int blk = d >> 5, s = (d >> 4) & 1, t = (d >> 2) & 3, e = d & 3;
-  return blk * 32 + s * 16 + (e < 2 ? 2 * t + e : 2 * t + 6 + e);
+// Q8_0 QK^T runs on the integer tensor path: q is quantised per head to
+// int8 hi + lo/254 (scale max|q| / 127), hi in A rows 0-7 and lo in rows
+// 8-15, one m16n8k32 MMA per 32-element Q8_0 block.  A thread's B fragment
+// is then the 8 consecutive K bytes 8t..8t+7 of its block (MMA k 4t..4t+3
+// and 16+4t..16+4t+3), so q follows the same order: byte d of head h goes to
+// the fragment word of lane 4h + t that MMA k index of d falls in.  The
+// fragments sit in lane order, [block][lane][4 words], one 16-byte load each.
+__device__ __forceinline__ int q8_frag_byte(int h, int d, bool lo) {
+  const int blk = d >> 5, w = d & 31, t = w >> 3, half = (w >> 2) & 1;
+  return ((blk * 32 + h * 4 + t) * 4 + 2 * half + (lo ? 1 : 0)) * 4 + (d & 3);
 }
 
 __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
@@ -601,33 +608,78 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     __syncwarp();
     if (lane == 0) mbar_arrive(appended);
   }
-  // Rotated query rows of this KV head's group, split hi/lo: row g holds the
-  // high part of head g, row g+8 the remainder.
-  for (int idx = threadIdx.x; idx < 8 * (HD / 2); idx += NCT) {
-    const int hg = idx / (HD / 2), p = idx % (HD / 2);
-    float y0 = 0.f, y1 = 0.f;
-    if (hg < a.group) {
-      const size_t off = (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + 2 * p;
-      rope_pair(load_elem(a.q, off, a.in_dtype), load_elem(a.q, off + 1, a.in_dtype),
-                rope_cs<DEVROPE>(rsrc, p, HD), y0, y1);
+  // Rotated query rows of this KV head's group.  f16/bf16: split hi/lo, row
+  // g the high part of head g, row g+8 the remainder.  Q8_0: int8 fragments
+  // (q8_frag_byte) and the per-head factor that turns the integer dot
+  // products back into scores.
+  uint32_t* qfrag = reinterpret_cast<uint32_t*>(qs);                  // Q8_0: [HD/32][32][4]
+  float* qfac = reinterpret_cast<float*>(qfrag + (HD / 32) * 32 * 4);  // Q8_0: [8]
+  if constexpr (Q8) {
+    static_assert(KG == 1 && NCT == 128 && (HD / 2) % 32 == 0, "Q8_0 q staging layout");
+    constexpr int kIt = 8 * (HD / 2) / NCT;  // pairs per thread; a warp stays inside one head
+    float* qmax = qfac + 8;                   // [8 heads][HD / 64 warps]
+    float y[kIt][2];
+#pragma unroll
+    for (int it = 0; it < kIt; ++it) {
+      const int idx = threadIdx.x + it * NCT, hg = idx / (HD / 2), p = idx % (HD / 2);
+      y[it][0] = y[it][1] = 0.f;
+      if (hg < a.group) {
+        const size_t off = (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + 2 * p;
+        rope_pair(load_elem(a.q, off, a.in_dtype), load_elem(a.q, off + 1, a.in_dtype),
+                  rope_cs<DEVROPE>(rsrc, p, HD), y[it][0], y[it][1]);
+      }
+      float mx = fmaxf(fabsf(y[it][0]), fabsf(y[it][1]));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0) qmax[hg * (HD / 64) + p / 32] = mx;
     }
-    float h0, l0, h1, l1;
-    split16<BF>(y0, h0, l0);
-    split16<BF>(y1, h1, l1);
-    const int k0 = Q8 ? q8_logical_k(2 * p) : 2 * p;
-    const int k1 = Q8 ? q8_logical_k(2 * p + 1) : 2 * p + 1;
-    const uint32_t hh = pack2<BF>(h0, h1), ll = pack2<BF>(l0, l1);
-    qs[hg * C::kQLd + k0] = static_cast<uint16_t>(hh & 0xffff);
-    qs[hg * C::kQLd + k1] = static_cast<uint16_t>(hh >> 16);
-    qs[(hg + 8) * C::kQLd + k0] = static_cast<uint16_t>(ll & 0xffff);
-    qs[(hg + 8) * C::kQLd + k1] = static_cast<uint16_t>(ll >> 16);
+    bar_consumers<NCT>();
+#pragma unroll
+    for (int it = 0; it < kIt; ++it) {
+      const int idx = threadIdx.x + it * NCT, hg = idx / (HD / 2), p = idx % (HD / 2);
+      float mx = 0.f;
+#pragma unroll
+      for (int w = 0; w < HD / 64; ++w) mx = fmaxf(mx, qmax[hg * (HD / 64) + w]);
+      const float inv = mx > 0.f ? 127.f / mx : 0.f;
+      uint32_t hi2 = 0, lo2 = 0;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float u = y[it][e] * inv;  // |u| <= 127
+        const int h = __float2int_rn(u);
+        const int l = __float2int_rn((u - static_cast<float>(h)) * 254.f);  // |l| <= 127
+        hi2 |= (static_cast<uint32_t>(h) & 0xffu) << (8 * e);
+        lo2 |= (static_cast<uint32_t>(l) & 0xffu) << (8 * e);
+      }
+      uint8_t* fb = reinterpret_cast<uint8_t*>(qfrag);
+      *reinterpret_cast<uint16_t*>(fb + q8_frag_byte(hg, 2 * p, false)) = static_cast<uint16_t>(hi2);
+      *reinterpret_cast<uint16_t*>(fb + q8_frag_byte(hg, 2 * p, true)) = static_cast<uint16_t>(lo2);
+      if (p == 0) qfac[hg] = mx * (1.f / (127.f * 254.f));
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < 8 * (HD / 2); idx += NCT) {
+      const int hg = idx / (HD / 2), p = idx % (HD / 2);
+      float y0 = 0.f, y1 = 0.f;
+      if (hg < a.group) {
+        const size_t off = (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + 2 * p;
+        rope_pair(load_elem(a.q, off, a.in_dtype), load_elem(a.q, off + 1, a.in_dtype),
+                  rope_cs<DEVROPE>(rsrc, p, HD), y0, y1);
+      }
+      float h0, l0, h1, l1;
+      split16<BF>(y0, h0, l0);
+      split16<BF>(y1, h1, l1);
+      const uint32_t hh = pack2<BF>(h0, h1), ll = pack2<BF>(l0, l1);
+      qs[hg * C::kQLd + 2 * p] = static_cast<uint16_t>(hh & 0xffff);
+      qs[hg * C::kQLd + 2 * p + 1] = static_cast<uint16_t>(hh >> 16);
+      qs[(hg + 8) * C::kQLd + 2 * p] = static_cast<uint16_t>(ll & 0xffff);
+      qs[(hg + 8) * C::kQLd + 2 * p + 1] = static_cast<uint16_t>(ll >> 16);
+    }
   }
   bar_consumers<NCT>();
 
   // ----------------------------------------------------------- consumers --
-  // A fragments of q: k-step ks starts 32 bytes after k-step ks-1.  The f16
-  // and bf16 variants hold all of them in registers; Q8_0, whose int8
-  // conversion needs the registers, reloads each one from shared memory.
+  // A fragments of q (f16/bf16): k-step ks starts 32 bytes after k-step
+  // ks-1, all of them held in registers.  Q8_0 reloads its int8 fragments
+  // from shared memory, one 16-byte load per block.
   const uint32_t qaddr =
       smem_u32(qs + (((lane >> 3) & 1) * 8 + (lane & 7)) * C::kQLd + (lane >> 4) * 8);
   uint32_t qa[Q8 ? 1 : NKS][4];
@@ -642,6 +694,8 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   for (int j = 0; j < NO; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m = -CUDART_INF_F, l = 0.f;
   const float sl2 = a.scale * kLog2e;
+  // Q8_0 scores come out of the integer MMAs in units of this head's q scale / 254
+  const float sl2q = Q8 ? sl2 * qfac[g] : sl2;
 
   for (int i = grp; i < my_tiles; i += KG) {  // the group's tiles of this split
     const int st = i % C::kStages;
@@ -695,39 +749,40 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
         __syncwarp();
       }
       // ---- S = Q K^T over this warp's 16 positions (two n-tiles of 8)
-      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      float x[4];  // head g at positions 2tq, 2tq+1, 8+2tq, 9+2tq
       if constexpr (Q8) {
+        // One integer MMA per block and n-tile; 254 * hi + lo rows give the
+        // block's dot product, scaled by the positions' K scales.
         const uint16_t* ksc = reinterpret_cast<const uint16_t*>(sb + 2 * C::kKBytes);
+        uint2 sc[2][2];  // [n-tile][position]: the HD/32 block scales of one row
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+            sc[nt][e] = *reinterpret_cast<const uint2*>(ksc + (16 * slice + 8 * nt + 2 * tq + e) *
+                                                                  (HD / 32));
+        x[0] = x[1] = x[2] = x[3] = 0.f;
 #pragma unroll
         for (int blk = 0; blk < HD / 32; ++blk) {
-          float sb2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-#pragma unroll
-          for (int s2 = 0; s2 < 2; ++s2) {
-            uint32_t qf[4];
-            ldmatrix_x4(qaddr + (2 * blk + s2) * 32, qf[0], qf[1], qf[2], qf[3]);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-              const int r = 16 * slice + 8 * nt + g;
-              const int byte = 32 * blk + 16 * s2 + 4 * tq;
-              const uint32_t w =
-                  *reinterpret_cast<const uint32_t*>(sb + swz128(r, byte >> 4) + (byte & 15));
-              uint32_t b0, b1;
-              i8x4_to_h2x2(w, b0, b1);
-              mma16816<false>(sb2[nt], qf, b0, b1);
-            }
-          }
+          const uint4 qf = *reinterpret_cast<const uint4*>(qfrag + (blk * 32 + lane) * 4);
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
-            const int r0 = 16 * slice + 8 * nt + 2 * tq;
-            const float d0 = __half2float(__ushort_as_half(ksc[r0 * (HD / 32) + blk]));
-            const float d1 = __half2float(__ushort_as_half(ksc[(r0 + 1) * (HD / 32) + blk]));
-            s[nt][0] += d0 * sb2[nt][0];
-            s[nt][1] += d1 * sb2[nt][1];
-            s[nt][2] += d0 * sb2[nt][2];
-            s[nt][3] += d1 * sb2[nt][3];
+            const int r = 16 * slice + 8 * nt + g;
+            const int byte = 32 * blk + 8 * tq;
+            const uint2 kb = *reinterpret_cast<const uint2*>(sb + swz128(r, byte >> 4) + (byte & 15));
+            int c[4] = {0, 0, 0, 0};
+            mma16832_s8(c, qf, kb.x, kb.y);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const uint32_t w = blk < 2 ? sc[nt][e].x : sc[nt][e].y;
+              const float d = __half2float(__ushort_as_half(
+                  static_cast<uint16_t>((blk & 1) ? (w >> 16) : (w & 0xffffu))));
+              x[2 * nt + e] = fmaf(static_cast<float>(c[e] * 254 + c[e + 2]), d, x[2 * nt + e]);
+            }
           }
         }
       } else {
+        float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
         const uint32_t kbase = smem_u32(sb);
 #pragma unroll
         for (int ks = 0; ks < NKS; ++ks) {
@@ -738,14 +793,18 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
           mma16816<BF>(s[0], qa[ks], b0, b1);
           mma16816<BF>(s[1], qa[ks], b2, b3);
         }
+        // rows g and g+8 hold the high and low parts of head g
+        x[0] = s[0][0] + s[0][2];
+        x[1] = s[0][1] + s[0][3];
+        x[2] = s[1][0] + s[1][2];
+        x[3] = s[1][1] + s[1][3];
       }
       // ---- online softmax for head g over positions 2tq, 2tq+1, 8+2tq, 9+2tq
-      float x[4] = {s[0][0] + s[0][2], s[0][1] + s[0][3], s[1][0] + s[1][2], s[1][1] + s[1][3]};
       const int pp[4] = {2 * tq, 2 * tq + 1, 8 + 2 * tq, 9 + 2 * tq};
       float mx = -CUDART_INF_F;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        x[e] = pp[e] < valid ? x[e] * sl2 : -CUDART_INF_F;
+        x[e] = pp[e] < valid ? x[e] * sl2q : -CUDART_INF_F;
         mx = fmaxf(mx, x[e]);
       }
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
