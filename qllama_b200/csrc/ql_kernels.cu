@@ -359,6 +359,10 @@ __device__ __forceinline__ int q8_frag_byte(int h, int d, bool lo) {
   return ((blk * 32 + h * 4 + t) * 4 + 2 * half + (lo ? 1 : 0)) * 4 + (d & 3);
 }
 
+// Decode softmax: the running maximum used as reference lags the true one by
+// at most this much (log2 units), so probabilities stay below 2^8.
+constexpr float kLazyLog2 = 8.f;
+
 __device__ __forceinline__ uint32_t swz128(int row, int chunk) {
   // byte offset of 16-byte chunk `chunk` (0..7) of row `row` in a 128B-swizzled box
   return static_cast<uint32_t>(row * 128 + (((chunk ^ (row & 7))) << 4));
@@ -809,9 +813,14 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
       }
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float m_new = fmaxf(m, mx);
-      const float base = m_new == -CUDART_INF_F ? 0.f : m_new;
-      const float corr = exp2f(m - base);
+      // The reference maximum moves only when the tile's maximum exceeds it
+      // by more than 2^kLazyLog2, so P stays below 2^kLazyLog2 and (m, l, O)
+      // stay consistent; the rescale of O then happens a few times per split
+      // instead of whenever one of the eight heads sees a new maximum.
+      const bool bump = mx > m + kLazyLog2;  // always taken while m is -inf and mx is not
+      const float corr = bump ? exp2f(m - mx) : 1.f;  // 0 when m was -inf
+      if (bump) m = mx;
+      const float base = m == -CUDART_INF_F ? 0.f : m;
       float p[4], psum = 0.f;
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -819,10 +828,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
         psum += p[e];
       }
       l = l * corr + psum;
-      m = m_new;
-      // corr is exactly 1 while the running maximum stays put, the usual case
-      // past the first tiles; the warp then skips the rescale.
-      if (__any_sync(0xffffffffu, corr != 1.f)) {
+      if (__any_sync(0xffffffffu, bump)) {
 #pragma unroll
         for (int j = 0; j < NO; ++j) {
           o[j][0] *= corr;
