@@ -89,20 +89,29 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
 // ------------------------------------------------- thread-block clusters --
 // Split arrive/wait of the hardware cluster barrier (every thread of every CTA
 // arrives once, right after its mbarriers are initialised; waiting later
-// costs nothing), a remote arrive on another CTA's mbarrier with release at
-// cluster scope, and a bounded wait that acquires at cluster scope.
+// costs nothing), stores into another CTA's shared memory that complete on
+// its mbarrier, and a bounded wait that acquires at cluster scope.
 __device__ __forceinline__ void cluster_arrive_relaxed() {
   asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait;" ::: "memory");
 }
-__device__ __forceinline__ void mbar_arrive_remote(uint64_t* bar, uint32_t cta_rank) {
+// Address of the same shared-memory location in CTA `cta_rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t cta_rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(cta_rank));
+  return r;
+}
+// Asynchronous 16-byte store into another CTA's shared memory (both
+// addresses from mapa_shared) whose completion counts 16 bytes on that CTA's
+// mbarrier; the issuing thread does not wait for it.
+__device__ __forceinline__ void st_async_v4(uint32_t remote_addr, const float4& v,
+                                            uint32_t remote_bar) {
   asm volatile(
-      "{\n\t.reg .b32 ra;\n\t"
-      "mapa.shared::cluster.u32 ra, %0, %1;\n\t"
-      "mbarrier.arrive.release.cluster.shared::cluster.b64 _, [ra];\n\t}" ::"r"(smem_u32(bar)),
-      "r"(cta_rank)
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::
+          "r"(remote_addr),
+      "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar)
       : "memory");
 }
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,

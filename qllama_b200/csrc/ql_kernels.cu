@@ -18,7 +18,6 @@
 //                   sequential f32 P.V) so its results track the reference to
 //                   the last bit in all but rare f64-exp rounding cases.
 //  gather_kernel    KvCache::get (cache.rs:185-229) into f32.
-#include <cooperative_groups.h>
 #include <math_constants.h>
 
 #include <algorithm>
@@ -330,9 +329,9 @@ struct SplitCfg {
   // regular layout; only clustered launches request these bytes.
   static constexpr int kMaxCluster = 8;  // portable cluster size
   static constexpr size_t kGatherOff = (kSmem - 1024 + 15) / 16 * 16;
-  // rows [rank][8][HD], (max, sum) [rank][16], weights [rank][8], then rank
-  // 0's arrival mbarrier
-  static constexpr size_t kGatherBytes = (kMaxCluster * 8 * HD + kMaxCluster * 24) * 4 + 16;
+  // rows [rank][8][HD], (max, sum) [rank][16], then rank 0's mbarrier that
+  // counts the bytes the other CTAs store
+  static constexpr size_t kGatherBytes = (kMaxCluster * 8 * HD + kMaxCluster * 16) * 4 + 16;
   static constexpr size_t kSmemCluster = 1024 + kGatherOff + kGatherBytes;
   // warp partials [warps][8][HD], the output rows [8][HD], (max, sum) [8][2] and
   // the per-(warp, head) weights [warps][8], f32
@@ -475,17 +474,13 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   const bool cl = a.cluster > 1;
   float* grows = reinterpret_cast<float*>(smem + C::kGatherOff);  // rank 0: [rank][8][HD]
   float* gml = grows + C::kMaxCluster * 8 * HD;                    // [rank][16] (max, sum)
-  float* gw = gml + C::kMaxCluster * 16;                           // [rank][8] weights
-  uint64_t* gbar = reinterpret_cast<uint64_t*>(gw + C::kMaxCluster * 8);  // the others arrive
+  uint64_t* gbar = reinterpret_cast<uint64_t*>(gml + C::kMaxCluster * 16);  // counts their bytes
 
   if (split >= nsplit) {
-    if (cl) {  // nothing to give rank 0 but the arrival it counts
-      cluster_arrive_relaxed();
-      if (threadIdx.x == 0) {
-        cluster_wait();  // rank 0's mbarrier is initialised
-        mbar_arrive_remote(gbar, 0);
-      }
-    }
+    // In a clustered launch such a CTA sends rank 0 nothing (rank 0 expects
+    // the bytes of the live splits only); it still arrives on the cluster
+    // barrier that the others wait on.
+    if (cl) cluster_arrive_relaxed();
     if (a.peer.nranks) {  // still counted, once the previous call is done with the counters
       griddep_wait();
       if (threadIdx.x == 0) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
@@ -517,7 +512,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
       mbar_init(&empty[s], 4);
     }
     mbar_init(appended, 1);
-    if (cl && split == 0) mbar_init(gbar, a.cluster - 1);
+    if (cl && split == 0) mbar_init(gbar, 1);  // rank 0's expect_tx; the bytes complete it
     fence_mbar_init();
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
@@ -921,102 +916,95 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   }
   bar_consumers<NCT>();
   const int tid = threadIdx.x;
-  float* wt = cml + 16;  // [NCW][8]
-  if (tid < 8) {
-    float M = -CUDART_INF_F;
-#pragma unroll
-    for (int w = 0; w < NCW; ++w) M = fmaxf(M, ml[(w * 8 + tid) * 2]);
-    const float Mb = M == -CUDART_INF_F ? 0.f : M;
-    float Lh = 0.f;
-    for (int w = 0; w < NCW; ++w) {
-      const float e = exp2f(ml[(w * 8 + tid) * 2] - Mb);
-      wt[w * 8 + tid] = e;
-      Lh += ml[(w * 8 + tid) * 2 + 1] * e;
-    }
-    const float inv = Lh > 0.f ? 1.f / Lh : 0.f;
-    for (int w = 0; w < NCW; ++w) wt[w * 8 + tid] *= inv;
-    cml[2 * tid] = M;
-    cml[2 * tid + 1] = Lh;
-  }
-  bar_consumers<NCT>();
   const size_t pslot = (static_cast<size_t>(job) * hkv + kvh) * a.max_splits;
+  // Each thread forms its head's weights itself (a few exponentials, no
+  // serial step and no barrier) and sums four columns over the warps.
   for (int c = tid; c < a.group * (HD / 4); c += NCT) {
     const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
+    float M = -CUDART_INF_F;
+#pragma unroll
+    for (int w = 0; w < NCW; ++w) M = fmaxf(M, ml[(w * 8 + hg) * 2]);
+    const float Mb = M == -CUDART_INF_F ? 0.f : M;
+    float Lh = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int w = 0; w < NCW; ++w) {
+      const float e = exp2f(ml[(w * 8 + hg) * 2] - Mb);
+      Lh = fmaf(ml[(w * 8 + hg) * 2 + 1], e, Lh);
       const float4 v = *reinterpret_cast<const float4*>(ob + (w * 8 + hg) * HD + d0);
-      const float ww = wt[w * 8 + hg];
-      acc.x += v.x * ww;
-      acc.y += v.y * ww;
-      acc.z += v.z * ww;
-      acc.w += v.w * ww;
+      acc.x = fmaf(v.x, e, acc.x);
+      acc.y = fmaf(v.y, e, acc.y);
+      acc.z = fmaf(v.z, e, acc.z);
+      acc.w = fmaf(v.w, e, acc.w);
     }
+    const float inv = Lh > 0.f ? 1.f / Lh : 0.f;
+    acc.x *= inv;
+    acc.y *= inv;
+    acc.z *= inv;
+    acc.w *= inv;
     if (nsplit == 1 || cl) {
       *reinterpret_cast<float4*>(res + hg * HD + d0) = acc;
+      if (d0 == 0) {
+        cml[2 * hg] = M;
+        cml[2 * hg + 1] = Lh;
+      }
     } else {
       *reinterpret_cast<float4*>(a.part_o + ((pslot + split) * 8 + hg) * HD + d0) = acc;
       if (d0 == 0) {
-        a.part_ml[((pslot + split) * 8 + hg) * 2] = cml[2 * hg];
-        a.part_ml[((pslot + split) * 8 + hg) * 2 + 1] = cml[2 * hg + 1];
+        a.part_ml[((pslot + split) * 8 + hg) * 2] = M;
+        a.part_ml[((pslot + split) * 8 + hg) * 2 + 1] = Lh;
       }
     }
   }
   if (cl) {
-    bar_consumers<NCT>();  // res is complete
+    // Rows of split r travel to rank 0 by asynchronous remote stores that
+    // count their bytes on rank 0's mbarrier; rank 0 expects the bytes of
+    // every live split but itself.
+    constexpr uint32_t kPushRow = HD * 4;
+    const uint32_t push_bytes = a.group * kPushRow + 16 * 4;
+    bar_consumers<NCT>();  // res and cml are complete
     if (split != 0) {
-      // Push this split's rows and (max, sum) into rank 0's shared memory,
-      // then count on rank 0's mbarrier; nothing reads this CTA afterwards.
-      namespace cgr = cooperative_groups;
-      cgr::cluster_group cluster = cgr::this_cluster();
-      float* drow = cluster.map_shared_rank(grows, 0) + split * 8 * HD;
-      float* dml = cluster.map_shared_rank(gml, 0) + split * 16;
+      cluster_wait();  // rank 0's mbarrier is initialised
+      const uint32_t rbar = mapa_shared(smem_u32(gbar), 0);
+      const uint32_t drow = mapa_shared(smem_u32(grows + split * 8 * HD), 0);
+      const uint32_t dml = mapa_shared(smem_u32(gml + split * 16), 0);
       for (int i = tid; i < a.group * HD / 4; i += NCT)
-        reinterpret_cast<float4*>(drow)[i] = reinterpret_cast<const float4*>(res)[i];
-      if (tid < 16) dml[tid] = cml[tid];
-      bar_consumers<NCT>();  // every push is issued before the release below
-      if (tid == 0) {
-        cluster_wait();  // rank 0's mbarrier is initialised
-        mbar_arrive_remote(gbar, 0);
-        if (a.peer.nranks) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
-      }
+        st_async_v4(drow + 16 * i, reinterpret_cast<const float4*>(res)[i], rbar);
+      if (tid < 4) st_async_v4(dml + 16 * tid, reinterpret_cast<const float4*>(cml)[tid], rbar);
+      if (tid == 0 && a.peer.nranks) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
       return;
     }
-    // Rank 0: every other CTA has pushed (bounded wait, acquire at cluster
-    // scope); merge the live splits by LSE weight.
+    // Rank 0: the other splits' rows have landed (bounded wait, acquire at
+    // cluster scope); merge the live splits by LSE weight, each thread
+    // forming its head's weights.
+    if (tid == 0) mbar_arrive_expect_tx(gbar, (nsplit - 1) * push_bytes);
     mbar_wait_cluster(gbar, 0, a.status);
-    if (tid < a.group) {
-      float M = cml[2 * tid];
-      for (int r = 1; r < nsplit; ++r) M = fmaxf(M, gml[r * 16 + 2 * tid]);
-      const float Mb = M == -CUDART_INF_F ? 0.f : M;
-      float den = 0.f;
-      for (int r = 0; r < nsplit; ++r) {
-        const float mr = r == 0 ? cml[2 * tid] : gml[r * 16 + 2 * tid];
-        const float lr = r == 0 ? cml[2 * tid + 1] : gml[r * 16 + 2 * tid + 1];
-        const float w = lr * exp2f(mr - Mb);
-        gw[r * 8 + tid] = w;
-        den += w;
-      }
-      const float inv = den > 0.f ? 1.f / den : 0.f;
-      for (int r = 0; r < nsplit; ++r) gw[r * 8 + tid] *= inv;
-    }
-    bar_consumers<NCT>();
     for (int c = tid; c < a.group * (HD / 4); c += NCT) {
       const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
+      float M = cml[2 * hg];
+      for (int r = 1; r < nsplit; ++r) M = fmaxf(M, gml[r * 16 + 2 * hg]);
+      const float Mb = M == -CUDART_INF_F ? 0.f : M;
+      const float w0 = cml[2 * hg + 1] * exp2f(cml[2 * hg] - Mb);
+      float den = w0;
       float4 acc = *reinterpret_cast<const float4*>(res + hg * HD + d0);
-      const float w0 = gw[hg];
       acc.x *= w0;
       acc.y *= w0;
       acc.z *= w0;
       acc.w *= w0;
       for (int r = 1; r < nsplit; ++r) {
+        const float w = gml[r * 16 + 2 * hg + 1] * exp2f(gml[r * 16 + 2 * hg] - Mb);
+        den += w;
         const float4 v = *reinterpret_cast<const float4*>(grows + (r * 8 + hg) * HD + d0);
-        const float ww = gw[r * 8 + hg];
-        acc.x += v.x * ww;
-        acc.y += v.y * ww;
-        acc.z += v.z * ww;
-        acc.w += v.w * ww;
+        acc.x = fmaf(v.x, w, acc.x);
+        acc.y = fmaf(v.y, w, acc.y);
+        acc.z = fmaf(v.z, w, acc.z);
+        acc.w = fmaf(v.w, w, acc.w);
       }
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      acc.x *= inv;
+      acc.y *= inv;
+      acc.z *= inv;
+      acc.w *= inv;
       *reinterpret_cast<float4*>(res + hg * HD + d0) = acc;
     }
     bar_consumers<NCT>();
