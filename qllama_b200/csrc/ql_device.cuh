@@ -104,7 +104,7 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t cta_rank
   return r;
 }
 // Asynchronous 16-byte store into another CTA's shared memory (both
-// addresses from mapa_shared) whose completion counts 16 bytes on that CTA's
+// addresses from mapa_shared) whose completion counts its bytes on that CTA's
 // mbarrier; the issuing thread does not wait for it.
 __device__ __forceinline__ void st_async_v4(uint32_t remote_addr, const float4& v,
                                             uint32_t remote_bar) {
@@ -157,6 +157,24 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// L2 prefetches: a 128-byte line, one box of a tensor map, or a plain range
+// (16-byte aligned, a multiple of 16 bytes).  The L2 is the GPU's point of
+// coherence, so a line fetched early is updated there by later writes.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
+__device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)),
+               "r"(bytes)
+               : "memory");
 }
 
 // 2-D tiled load of one box into shared memory, completing on `bar`.
@@ -256,6 +274,21 @@ __device__ __forceinline__ float load_elem(const void* base, size_t i, int dt) {
   if (dt == kF32) return static_cast<const float*>(base)[i];
   if (dt == kF16) return __half2float(static_cast<const __half*>(base)[i]);
   return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]);
+}
+
+// Elements i and i+1 (i even) in one access when `vec` says the base pointer
+// is aligned to two elements, else one at a time.
+__device__ __forceinline__ float2 load_pair(const void* base, size_t i, int dt, bool vec) {
+  if (!vec) return make_float2(load_elem(base, i, dt), load_elem(base, i + 1, dt));
+  if (dt == kF32) return *reinterpret_cast<const float2*>(static_cast<const float*>(base) + i);
+  if (dt == kF16)
+    return __half22float2(*reinterpret_cast<const __half2*>(static_cast<const __half*>(base) + i));
+  return __bfloat1622float2(
+      *reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(base) + i));
+}
+
+__device__ __forceinline__ bool pair_aligned(const void* base, int dt) {
+  return (reinterpret_cast<uintptr_t>(base) & (dt == kF32 ? 7u : 3u)) == 0;
 }
 
 __device__ __forceinline__ void store_elem(void* base, size_t i, int dt, float x) {

@@ -66,15 +66,14 @@ __device__ __forceinline__ double2 rope_cs(const RopeSrc& r, int p, int hd) {
 }
 
 // One warp writes one cache row (one position of one KV head): K rotated
-// when a rotation source is given, V as is, both converted to the cache type.
-// With `stage`, the same bytes also go to shared memory as
-// [K row][V row][K scales][V scales] (the scales for Q8_0 only).
-template <bool DEV>
-__device__ void append_row_t(const void* kin, const void* vin, int in_dt, size_t in_off,
-                             const RopeSrc& rope, bool rotate, const CacheView& c, int64_t dst,
-                             int lane, uint8_t* stage = nullptr) {
+// by the table row when one is given, V as is, both converted to the cache
+// type.
+__device__ __forceinline__ void append_row(const void* kin, const void* vin, int in_dt,
+                                           size_t in_off, const double2* rope_row,
+                                           const CacheView& c, int64_t dst, int lane) {
   const int hd = c.hd;
   const int pairs = hd / 2;
+  const RopeSrc rope{rope_row, 0.0, 0.0};
   for (int base = 0; base < pairs; base += 32) {
     const int p = base + lane;
     const bool valid = p < pairs;
@@ -84,7 +83,7 @@ __device__ void append_row_t(const void* kin, const void* vin, int in_dt, size_t
       k1 = load_elem(kin, in_off + 2 * p + 1, in_dt);
       v0 = load_elem(vin, in_off + 2 * p, in_dt);
       v1 = load_elem(vin, in_off + 2 * p + 1, in_dt);
-      if (rotate) rope_pair(k0, k1, rope_cs<DEV>(rope, p, hd), k0, k1);
+      if (rope_row) rope_pair(k0, k1, rope_cs<false>(rope, p, hd), k0, k1);
     }
     const size_t e = static_cast<size_t>(dst) * hd + 2 * p;
     if (c.dtype == kQ8_0) {
@@ -100,36 +99,14 @@ __device__ void append_row_t(const void* kin, const void* vin, int in_dt, size_t
           c.k_scale[si] = __half_as_ushort(sk);
           c.v_scale[si] = __half_as_ushort(sv);
         }
-        if (stage) {
-          *reinterpret_cast<char2*>(stage + 2 * p) = make_char2(qk0, qk1);
-          *reinterpret_cast<char2*>(stage + hd + 2 * p) = make_char2(qv0, qv1);
-          if ((lane & 15) == 0) {
-            uint16_t* ss = reinterpret_cast<uint16_t*>(stage + 2 * hd);
-            ss[(2 * p) / 32] = __half_as_ushort(sk);
-            ss[hd / 32 + (2 * p) / 32] = __half_as_ushort(sv);
-          }
-        }
       }
     } else if (valid) {
       store_elem(c.k, e, c.dtype, k0);
       store_elem(c.k, e + 1, c.dtype, k1);
       store_elem(c.v, e, c.dtype, v0);
       store_elem(c.v, e + 1, c.dtype, v1);
-      if (stage && c.dtype != kF32) {
-        const uint32_t kk = c.dtype == kF16 ? pack2<false>(k0, k1) : pack2<true>(k0, k1);
-        const uint32_t vv = c.dtype == kF16 ? pack2<false>(v0, v1) : pack2<true>(v0, v1);
-        reinterpret_cast<uint32_t*>(stage)[p] = kk;
-        reinterpret_cast<uint32_t*>(stage + 2 * hd)[p] = vv;
-      }
     }
   }
-}
-
-__device__ __forceinline__ void append_row(const void* kin, const void* vin, int in_dt,
-                                           size_t in_off, const double2* rope_row,
-                                           const CacheView& c, int64_t dst, int lane) {
-  append_row_t<false>(kin, vin, in_dt, in_off, RopeSrc{rope_row, 0.0, 0.0}, rope_row != nullptr,
-                      c, dst, lane);
 }
 
 __device__ __forceinline__ float cache_value(const CacheView& c, const void* base,
@@ -358,6 +335,85 @@ __device__ __forceinline__ int q8_frag_byte(int h, int d, bool lo) {
   return ((blk * 32 + h * 4 + t) * 4 + 2 * half + (lo ? 1 : 0)) * 4 + (d & 3);
 }
 
+// The decode kernel's fused append of the new token's row (one warp): all
+// loads first, then the converted row into shared memory and the release of
+// the consumers, then the same bytes into the cache.  Same conversion as
+// append_row_t; the cache is f16, bf16 or Q8_0 here.
+template <int HD, bool DEV>
+__device__ __forceinline__ void append_fused(const AttnArgs& a, const RopeSrc& rope,
+                                             size_t in_off, bool ok, int64_t dst, int lane,
+                                             uint8_t* stage, uint64_t* released) {
+  static_assert(HD % 64 == 0, "whole pairs per lane");
+  constexpr int kIt = HD / 64;  // pairs per lane
+  const bool kvec = pair_aligned(a.k, a.in_dtype), vvec = pair_aligned(a.v, a.in_dtype);
+  float2 kx[kIt], vx[kIt];
+  double2 cs[kIt];
+#pragma unroll
+  for (int it = 0; it < kIt; ++it) {
+    const int p = it * 32 + lane;
+    kx[it] = load_pair(a.k, in_off + 2 * p, a.in_dtype, kvec);
+    vx[it] = load_pair(a.v, in_off + 2 * p, a.in_dtype, vvec);
+    cs[it] = rope_cs<DEV>(rope, p, HD);
+  }
+#pragma unroll
+  for (int it = 0; it < kIt; ++it) rope_pair(kx[it].x, kx[it].y, cs[it], kx[it].x, kx[it].y);
+  const CacheView& c = a.cache;
+  if (c.dtype == kQ8_0) {
+    int8_t qk[kIt][2], qv[kIt][2];
+    __half sk[kIt], sv[kIt];
+#pragma unroll
+    for (int it = 0; it < kIt; ++it) {
+      q8_0_pair(kx[it].x, kx[it].y, qk[it][0], qk[it][1], sk[it]);
+      q8_0_pair(vx[it].x, vx[it].y, qv[it][0], qv[it][1], sv[it]);
+      const int p = it * 32 + lane;
+      *reinterpret_cast<char2*>(stage + 2 * p) = make_char2(qk[it][0], qk[it][1]);
+      *reinterpret_cast<char2*>(stage + HD + 2 * p) = make_char2(qv[it][0], qv[it][1]);
+      if ((lane & 15) == 0) {
+        uint16_t* ss = reinterpret_cast<uint16_t*>(stage + 2 * HD);
+        ss[(2 * p) / 32] = __half_as_ushort(sk[it]);
+        ss[HD / 32 + (2 * p) / 32] = __half_as_ushort(sv[it]);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(released);
+    if (ok) {
+#pragma unroll
+      for (int it = 0; it < kIt; ++it) {
+        const int p = it * 32 + lane;
+        const size_t e = static_cast<size_t>(dst) * HD + 2 * p;
+        *reinterpret_cast<char2*>(static_cast<int8_t*>(c.k) + e) = make_char2(qk[it][0], qk[it][1]);
+        *reinterpret_cast<char2*>(static_cast<int8_t*>(c.v) + e) = make_char2(qv[it][0], qv[it][1]);
+        if ((lane & 15) == 0) {
+          const size_t si = static_cast<size_t>(dst) * (HD / 32) + (2 * p) / 32;
+          c.k_scale[si] = __half_as_ushort(sk[it]);
+          c.v_scale[si] = __half_as_ushort(sv[it]);
+        }
+      }
+    }
+  } else {
+    const bool bf = c.dtype == kBF16;
+    uint32_t kk[kIt], vv[kIt];
+#pragma unroll
+    for (int it = 0; it < kIt; ++it) {
+      kk[it] = bf ? pack2<true>(kx[it].x, kx[it].y) : pack2<false>(kx[it].x, kx[it].y);
+      vv[it] = bf ? pack2<true>(vx[it].x, vx[it].y) : pack2<false>(vx[it].x, vx[it].y);
+      const int p = it * 32 + lane;
+      reinterpret_cast<uint32_t*>(stage)[p] = kk[it];
+      reinterpret_cast<uint32_t*>(stage + 2 * HD)[p] = vv[it];
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(released);
+    if (ok) {
+#pragma unroll
+      for (int it = 0; it < kIt; ++it) {
+        const size_t e = static_cast<size_t>(dst) * HD + 2 * (it * 32 + lane);
+        *reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(c.k) + e) = kk[it];
+        *reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(c.v) + e) = vv[it];
+      }
+    }
+  }
+}
+
 // Decode softmax: the running maximum used as reference lags the true one by
 // at most this much (log2 units), so probabilities stay below 2^8.
 constexpr float kLazyLog2 = 8.f;
@@ -525,6 +581,53 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   const int* bt = a.cache.block_table + static_cast<size_t>(seq) * a.cache.pages_per_seq;
   int lane_page = 0;
   if (warp == NCW && lane < my_tiles) lane_page = __ldg(bt + (tile0 + lane) * kTile / a.cache.page);
+  // What the CTA reads first once the dependency is met is fetched into L2
+  // now (prefetches read nothing into the CTA; lines written meanwhile are
+  // updated in L2): the first stages' tiles, q of this KV head's group, the
+  // rotation row and, for the appending CTA, the new K and V rows.
+  // The appending CTA's block-table entry for the new row, host-written too.
+  int app_page = -1;
+  if (warp == NCW && appends)
+    app_page = __ldg(bt + static_cast<size_t>(qpos) / a.cache.page);
+  if (warp == NCW) {
+    if (lane < min(my_tiles, C::kStages) && lane_page >= 0 && lane_page < a.cache.num_pages) {
+      const int row =
+          (lane_page * hkv + kvh) * a.cache.page + ((tile0 + lane) * kTile) % a.cache.page;
+      if constexpr (Q8) {
+        tma_prefetch_2d(&kmap, 0, row);
+        tma_prefetch_2d(&vmap, 0, row);
+        bulk_prefetch_l2(a.cache.k_scale + static_cast<size_t>(row) * (HD / 32), C::kScaleBytes);
+        bulk_prefetch_l2(a.cache.v_scale + static_cast<size_t>(row) * (HD / 32), C::kScaleBytes);
+      } else {
+#pragma unroll
+        for (int box = 0; box < HD / 64; ++box) {
+          tma_prefetch_2d(&kmap, box * 64, row);
+          tma_prefetch_2d(&vmap, box * 64, row);
+        }
+      }
+    }
+  } else if (warp < 4) {
+    const int ib = a.in_dtype == kF32 ? 4 : 2;
+    const size_t kv_off = (static_cast<size_t>(job) * hkv + kvh) * HD * ib;
+    const char* base = nullptr;
+    int bytes = 0;
+    if (warp == 0) {
+      base = static_cast<const char*>(a.q) +
+             (static_cast<size_t>(job) * a.hq + kvh * a.group) * HD * ib;
+      bytes = a.group * HD * ib;
+    } else if (warp == 1 && !DEVROPE) {
+      base = reinterpret_cast<const char*>(a.rope + static_cast<size_t>(qpos) * (HD / 2));
+      bytes = HD / 2 * 16;
+    } else if (warp >= 2 && appends) {
+      base = static_cast<const char*>(warp == 2 ? a.k : a.v) + kv_off;
+      bytes = HD * ib;
+    }
+    if (bytes > 0) {
+      const uintptr_t l0 = reinterpret_cast<uintptr_t>(base) & ~static_cast<uintptr_t>(127);
+      const int lines = static_cast<int>((reinterpret_cast<uintptr_t>(base) + bytes - l0 + 127) / 128);
+      for (int t = lane; t < lines; t += 32) prefetch_l2(reinterpret_cast<const void*>(l0 + 128 * t));
+    }
+  }
   // Programmatic dependent launch: everything above overlaps the previous
   // kernel; Q/K/V and the cache may come from it, so they are read only after
   // this wait.  The next kernel may start its own set-up from here on.
@@ -574,7 +677,25 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     // global load sits between two copies; lane 0 waits for free stages and
     // issues.  The tile holding the new token is copied at once too: its new
     // row is patched in shared memory by the consumers.
-    bool alive = true;
+    // Single-token decode: the CTA holding the last tile writes the new K/V
+    // row (rotated K) to the cache and to shared memory, then releases the
+    // consumer warp that patches it into its tile.  The producer does this
+    // right after its first burst of copies, while the consumers rotate q.
+    // The consumers need only the shared-memory row, so they are released
+    // before the proxy fence that orders the cache writes before later TMA
+    // reads (the fence may wait for this warp's copies in flight).
+    auto append_new_row = [&]() {
+      const bool ok = app_page >= 0 && app_page < a.cache.num_pages;
+      if (!ok && lane == 0) atomicOr(a.status, kStatusBadPage);
+      const int64_t dst =
+          ok ? (static_cast<int64_t>(app_page) * hkv + kvh) * a.cache.page + qpos % a.cache.page
+             : 0;
+      append_fused<HD, DEVROPE>(a, rsrc, (static_cast<size_t>(job) * hkv + kvh) * HD, ok, dst,
+                                lane, newrow, appended);
+      fence_proxy_async_global();
+    };
+    bool alive = true, append_due = appends;
+    const int burst = min(my_tiles, C::kStages);
     for (int i0 = 0; i0 < my_tiles && alive; i0 += 32) {
       if (i0 > 0)
         lane_page = i0 + lane < my_tiles ? __ldg(bt + (tile0 + i0 + lane) * kTile / a.cache.page)
@@ -590,23 +711,16 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
             issue(i, page);
         }
         alive = __shfl_sync(0xffffffffu, alive, 0);
+        if (append_due && i0 + j + 1 == burst) {
+          append_new_row();
+          append_due = false;
+        }
       }
     }
+    if (append_due) append_new_row();  // the copies stopped early; still release the consumers
     return;
   }
 
-  // Single-token decode: the CTA holding the last tile writes the new K/V
-  // (rotated K) and releases the producer for that tile.
-  if (appends && warp == 0) {
-    bool ok;
-    const int64_t dst = cache_row(a.cache, seq, qpos, kvh, a.status, ok);
-    if (ok)
-      append_row_t<DEVROPE>(a.k, a.v, a.in_dtype, (static_cast<size_t>(job) * hkv + kvh) * HD,
-                            rsrc, true, a.cache, dst, lane, newrow);
-    fence_proxy_async_global();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(appended);
-  }
   // Rotated query rows of this KV head's group.  f16/bf16: split hi/lo, row
   // g the high part of head g, row g+8 the remainder.  Q8_0: int8 fragments
   // (q8_frag_byte) and the per-head factor that turns the integer dot
@@ -981,20 +1095,33 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     mbar_wait_cluster(gbar, 0, a.status);
     for (int c = tid; c < a.group * (HD / 4); c += NCT) {
       const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
-      float M = cml[2 * hg];
-      for (int r = 1; r < nsplit; ++r) M = fmaxf(M, gml[r * 16 + 2 * hg]);
+      // unrolled over the largest cluster with predicated loads, so that all
+      // of them issue at once; splits past nsplit weigh 0
+      float mr[C::kMaxCluster], lr[C::kMaxCluster];
+      mr[0] = cml[2 * hg];
+      lr[0] = cml[2 * hg + 1];
+      float M = mr[0];
+#pragma unroll
+      for (int r = 1; r < C::kMaxCluster; ++r) {
+        mr[r] = r < nsplit ? gml[r * 16 + 2 * hg] : -CUDART_INF_F;
+        lr[r] = r < nsplit ? gml[r * 16 + 2 * hg + 1] : 0.f;
+        M = fmaxf(M, mr[r]);
+      }
       const float Mb = M == -CUDART_INF_F ? 0.f : M;
-      const float w0 = cml[2 * hg + 1] * exp2f(cml[2 * hg] - Mb);
+      const float w0 = lr[0] * exp2f(mr[0] - Mb);
       float den = w0;
       float4 acc = *reinterpret_cast<const float4*>(res + hg * HD + d0);
       acc.x *= w0;
       acc.y *= w0;
       acc.z *= w0;
       acc.w *= w0;
-      for (int r = 1; r < nsplit; ++r) {
-        const float w = gml[r * 16 + 2 * hg + 1] * exp2f(gml[r * 16 + 2 * hg] - Mb);
+#pragma unroll
+      for (int r = 1; r < C::kMaxCluster; ++r) {
+        const float w = lr[r] * exp2f(mr[r] - Mb);
         den += w;
-        const float4 v = *reinterpret_cast<const float4*>(grows + (r * 8 + hg) * HD + d0);
+        const float4 v = r < nsplit
+                             ? *reinterpret_cast<const float4*>(grows + (r * 8 + hg) * HD + d0)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
         acc.x = fmaf(v.x, w, acc.x);
         acc.y = fmaf(v.y, w, acc.y);
         acc.z = fmaf(v.z, w, acc.z);
