@@ -414,6 +414,46 @@ __device__ __forceinline__ void append_fused(const AttnArgs& a, const RopeSrc& r
   }
 }
 
+// Pairs (2p, 2p+1) of the q rows of one KV head's group, item idx = tid +
+// it * NCT -> head idx / (HD/2), pair idx % (HD/2) (zero past the group).
+// The input type is resolved once, outside the loads, so that every load is
+// issued before the first is used.
+template <int N, int NCT, int HD, typename LD>
+__device__ __forceinline__ void gather_q_pairs(int group, size_t row0, int tid, float2 (&x)[N],
+                                               LD ld) {
+#pragma unroll
+  for (int it = 0; it < N; ++it) {
+    const int idx = tid + it * NCT, hg = idx / (HD / 2), p = idx % (HD / 2);
+    x[it] = idx < 8 * (HD / 2) && hg < group ? ld(row0 + static_cast<size_t>(hg) * HD + 2 * p)
+                                             : make_float2(0.f, 0.f);
+  }
+}
+
+template <int N, int NCT, int HD>
+__device__ __forceinline__ void load_q_pairs(const AttnArgs& a, size_t row0, int tid,
+                                             float2 (&x)[N]) {
+  const void* q = a.q;
+  if (a.in_dtype == kF16 && pair_aligned(q, kF16)) {
+    gather_q_pairs<N, NCT, HD>(a.group, row0, tid, x, [q](size_t i) {
+      return __half22float2(*reinterpret_cast<const __half2*>(static_cast<const __half*>(q) + i));
+    });
+  } else if (a.in_dtype == kBF16 && pair_aligned(q, kBF16)) {
+    gather_q_pairs<N, NCT, HD>(a.group, row0, tid, x, [q](size_t i) {
+      return __bfloat1622float2(
+          *reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(q) + i));
+    });
+  } else if (a.in_dtype == kF32 && pair_aligned(q, kF32)) {
+    gather_q_pairs<N, NCT, HD>(a.group, row0, tid, x, [q](size_t i) {
+      return *reinterpret_cast<const float2*>(static_cast<const float*>(q) + i);
+    });
+  } else {
+    const int dt = a.in_dtype;
+    gather_q_pairs<N, NCT, HD>(a.group, row0, tid, x, [q, dt](size_t i) {
+      return make_float2(load_elem(q, i, dt), load_elem(q, i + 1, dt));
+    });
+  }
+}
+
 // Decode softmax: the running maximum used as reference lags the true one by
 // at most this much (log2 units), so probabilities stay below 2^8.
 constexpr float kLazyLog2 = 8.f;
@@ -725,6 +765,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   // g the high part of head g, row g+8 the remainder.  Q8_0: int8 fragments
   // (q8_frag_byte) and the per-head factor that turns the integer dot
   // products back into scores.
+  const size_t qrow0 = (static_cast<size_t>(job) * a.hq + kvh * a.group) * HD;
   uint32_t* qfrag = reinterpret_cast<uint32_t*>(qs);                  // Q8_0: [HD/32][32][4]
   float* qfac = reinterpret_cast<float*>(qfrag + (HD / 32) * 32 * 4);  // Q8_0: [8]
   if constexpr (Q8) {
@@ -732,15 +773,13 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     constexpr int kIt = 8 * (HD / 2) / NCT;  // pairs per thread; a warp stays inside one head
     float* qmax = qfac + 8;                   // [8 heads][HD / 64 warps]
     float y[kIt][2];
+    float2 xq[kIt];
+    load_q_pairs<kIt, NCT, HD>(a, qrow0, threadIdx.x, xq);
 #pragma unroll
     for (int it = 0; it < kIt; ++it) {
       const int idx = threadIdx.x + it * NCT, hg = idx / (HD / 2), p = idx % (HD / 2);
       y[it][0] = y[it][1] = 0.f;
-      if (hg < a.group) {
-        const size_t off = (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + 2 * p;
-        rope_pair(load_elem(a.q, off, a.in_dtype), load_elem(a.q, off + 1, a.in_dtype),
-                  rope_cs<DEVROPE>(rsrc, p, HD), y[it][0], y[it][1]);
-      }
+      if (hg < a.group) rope_pair(xq[it].x, xq[it].y, rope_cs<DEVROPE>(rsrc, p, HD), y[it][0], y[it][1]);
       float mx = fmaxf(fabsf(y[it][0]), fabsf(y[it][1]));
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -769,14 +808,15 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
       if (p == 0) qfac[hg] = mx * (1.f / (127.f * 254.f));
     }
   } else {
-    for (int idx = threadIdx.x; idx < 8 * (HD / 2); idx += NCT) {
-      const int hg = idx / (HD / 2), p = idx % (HD / 2);
+    constexpr int kQIt = (8 * (HD / 2) + NCT - 1) / NCT;
+    float2 xq[kQIt];
+    load_q_pairs<kQIt, NCT, HD>(a, qrow0, threadIdx.x, xq);
+#pragma unroll
+    for (int it = 0; it < kQIt; ++it) {
+      const int idx = threadIdx.x + it * NCT, hg = idx / (HD / 2), p = idx % (HD / 2);
+      if (idx >= 8 * (HD / 2)) break;
       float y0 = 0.f, y1 = 0.f;
-      if (hg < a.group) {
-        const size_t off = (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + 2 * p;
-        rope_pair(load_elem(a.q, off, a.in_dtype), load_elem(a.q, off + 1, a.in_dtype),
-                  rope_cs<DEVROPE>(rsrc, p, HD), y0, y1);
-      }
+      if (hg < a.group) rope_pair(xq[it].x, xq[it].y, rope_cs<DEVROPE>(rsrc, p, HD), y0, y1);
       float h0, l0, h1, l1;
       split16<BF>(y0, h0, l0);
       split16<BF>(y1, h1, l1);
