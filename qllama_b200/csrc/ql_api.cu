@@ -817,20 +817,22 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
   // consumer groups share each split's tiles, one CTA per SM (latency).
   const int wide_kg = fast ? ql::splitkv_wide_groups(hd, kv->cfg.dtype) : 0;
   const bool latency = fast && 2LL * jobs * hkv <= c->num_sms;
-  // A short context in that regime: up to kMaxCluster CTAs of about
-  // kClusterTiles tiles each per job, as one thread-block cluster that merges
+  // A short context in that regime: each job's tiles spread over up to
+  // kMaxCluster CTAs (one tile each when every CTA of the launch then has an
+  // SM of its own, more otherwise), as one thread-block cluster that merges
   // through distributed shared memory (each CTA streams its tiles on its own
   // SM; one SM's TMA alone moves a few tens of GB/s).
-#ifndef QL_CLUSTER_TILES
-#define QL_CLUSTER_TILES 2
-#endif
-#ifndef QL_MAX_CLUSTER
-#define QL_MAX_CLUSTER 8
-#endif
-  constexpr int kMaxCluster = QL_MAX_CLUSTER, kClusterTiles = QL_CLUSTER_TILES;
-  static_assert(kMaxCluster <= 8, "the kernel's gather area holds 8 CTAs");
-  const int cluster_ctas = (max_tiles + kClusterTiles - 1) / kClusterTiles;
-  const bool clustered = latency && max_tiles > 1 && cluster_ctas <= kMaxCluster;
+  // Clusters above the portable 8 CTAs only while there are few of them, so
+  // that each finds a GPC with that many free SMs; at most 8 tiles per CTA
+  // (longer contexts use every SM through the kernels below).
+  const long long pairs = 1LL * jobs * hkv;
+  const int max_cluster = pairs <= 4 ? ql::kMaxClusterCtas : std::min(8, ql::kMaxClusterCtas);
+  const long long pair_tiles = 1LL * max_tiles * pairs;
+  const int cta_tiles = static_cast<int>(
+      std::max<long long>((pair_tiles + c->num_sms - 1) / c->num_sms,
+                          (max_tiles + max_cluster - 1) / max_cluster));
+  const int cluster_ctas = (max_tiles + cta_tiles - 1) / cta_tiles;
+  const bool clustered = latency && cluster_ctas >= 2 && cta_tiles <= 8;
   const bool wide = !clustered && latency && wide_kg > 0;
   int cluster = 0;
   if (clustered) {

@@ -22,6 +22,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <type_traits>
 
 #include "ql_device.cuh"
 #include "ql_kernels.cuh"
@@ -301,15 +302,18 @@ struct SplitCfg {
   static constexpr int kRowBytes = kQ8 ? 2 * HD + 2 * (HD / 32) * 2 : 4 * HD;
   static constexpr size_t kSmem = 1024 + static_cast<size_t>(kStages) * kStageBytes + kRowOff +
                                   (kRowBytes + 15) / 16 * 16;
-  // Cluster mode (KG == 1): rank 0's gather area for the other CTAs' rows
-  // [kMaxCluster][8][HD] and (max, sum) [kMaxCluster][8][2], f32, past the
-  // regular layout; only clustered launches request these bytes.
-  static constexpr int kMaxCluster = 8;  // portable cluster size
+  // Cluster mode (KG == 1): rank 0's gather area past the regular layout,
+  // for clusters of `ctas` CTAs: rows [ctas][8][HD] and (max, sum)
+  // [ctas][8][2], f32, then rank 0's mbarrier that counts the bytes the other
+  // CTAs store.  Only clustered launches request these bytes.
+  static constexpr int kMaxCluster = kMaxClusterCtas;
   static constexpr size_t kGatherOff = (kSmem - 1024 + 15) / 16 * 16;
-  // rows [rank][8][HD], (max, sum) [rank][16], then rank 0's mbarrier that
-  // counts the bytes the other CTAs store
-  static constexpr size_t kGatherBytes = (kMaxCluster * 8 * HD + kMaxCluster * 16) * 4 + 16;
-  static constexpr size_t kSmemCluster = 1024 + kGatherOff + kGatherBytes;
+  static constexpr size_t gather_bytes(int ctas) {
+    return (static_cast<size_t>(ctas) * 8 * HD + ctas * 16) * 4 + 16;
+  }
+  // a launch with clusters of `ctas` CTAs requests the gather area for that many
+  static constexpr size_t smem_cluster(int ctas) { return 1024 + kGatherOff + gather_bytes(ctas); }
+  static constexpr size_t kSmemCluster = smem_cluster(kMaxCluster);
   // warp partials [warps][8][HD], the output rows [8][HD], (max, sum) [8][2] and
   // the per-(warp, head) weights [warps][8], f32
   static_assert(((kConsumerWarps + 1) * 8 * HD + 16 + 8 * kConsumerWarps) * 4 <=
@@ -569,8 +573,8 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   // the cluster reaches both cluster barriers below on every path.
   const bool cl = a.cluster > 1;
   float* grows = reinterpret_cast<float*>(smem + C::kGatherOff);  // rank 0: [rank][8][HD]
-  float* gml = grows + C::kMaxCluster * 8 * HD;                    // [rank][16] (max, sum)
-  uint64_t* gbar = reinterpret_cast<uint64_t*>(gml + C::kMaxCluster * 16);  // counts their bytes
+  float* gml = grows + a.cluster * 8 * HD;                         // [rank][16] (max, sum)
+  uint64_t* gbar = reinterpret_cast<uint64_t*>(gml + a.cluster * 16);  // counts their bytes
 
   if (split >= nsplit) {
     // In a clustered launch such a CTA sends rank 0 nothing (rank 0 expects
@@ -1133,47 +1137,48 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     // forming its head's weights.
     if (tid == 0) mbar_arrive_expect_tx(gbar, (nsplit - 1) * push_bytes);
     mbar_wait_cluster(gbar, 0, a.status);
-    for (int c = tid; c < a.group * (HD / 4); c += NCT) {
-      const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
-      // unrolled over the largest cluster with predicated loads, so that all
-      // of them issue at once; splits past nsplit weigh 0
-      float mr[C::kMaxCluster], lr[C::kMaxCluster];
-      mr[0] = cml[2 * hg];
-      lr[0] = cml[2 * hg + 1];
-      float M = mr[0];
+    // Unrolled over 8 or over the largest cluster with predicated loads, so
+    // that all the loads issue at once; splits past nsplit weigh 0.
+    auto merge = [&](auto width) {
+      constexpr int N = decltype(width)::value;
+      for (int c = tid; c < a.group * (HD / 4); c += NCT) {
+        const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
+        float mr[N], lr[N];
+        float M = -CUDART_INF_F;
 #pragma unroll
-      for (int r = 1; r < C::kMaxCluster; ++r) {
-        mr[r] = r < nsplit ? gml[r * 16 + 2 * hg] : -CUDART_INF_F;
-        lr[r] = r < nsplit ? gml[r * 16 + 2 * hg + 1] : 0.f;
-        M = fmaxf(M, mr[r]);
-      }
-      const float Mb = M == -CUDART_INF_F ? 0.f : M;
-      const float w0 = lr[0] * exp2f(mr[0] - Mb);
-      float den = w0;
-      float4 acc = *reinterpret_cast<const float4*>(res + hg * HD + d0);
-      acc.x *= w0;
-      acc.y *= w0;
-      acc.z *= w0;
-      acc.w *= w0;
+        for (int r = 0; r < N; ++r) {
+          mr[r] = r == 0 ? cml[2 * hg] : (r < nsplit ? gml[r * 16 + 2 * hg] : -CUDART_INF_F);
+          lr[r] = r == 0 ? cml[2 * hg + 1] : (r < nsplit ? gml[r * 16 + 2 * hg + 1] : 0.f);
+          M = fmaxf(M, mr[r]);
+        }
+        const float Mb = M == -CUDART_INF_F ? 0.f : M;
+        float den = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int r = 1; r < C::kMaxCluster; ++r) {
-        const float w = lr[r] * exp2f(mr[r] - Mb);
-        den += w;
-        const float4 v = r < nsplit
-                             ? *reinterpret_cast<const float4*>(grows + (r * 8 + hg) * HD + d0)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-        acc.x = fmaf(v.x, w, acc.x);
-        acc.y = fmaf(v.y, w, acc.y);
-        acc.z = fmaf(v.z, w, acc.z);
-        acc.w = fmaf(v.w, w, acc.w);
+        for (int r = 0; r < N; ++r) {
+          const float w = lr[r] * exp2f(mr[r] - Mb);
+          den += w;
+          const float4 v =
+              r == 0 ? *reinterpret_cast<const float4*>(res + hg * HD + d0)
+                     : (r < nsplit ? *reinterpret_cast<const float4*>(grows + (r * 8 + hg) * HD + d0)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f));
+          acc.x = fmaf(v.x, w, acc.x);
+          acc.y = fmaf(v.y, w, acc.y);
+          acc.z = fmaf(v.z, w, acc.z);
+          acc.w = fmaf(v.w, w, acc.w);
+        }
+        const float inv = den > 0.f ? 1.f / den : 0.f;
+        acc.x *= inv;
+        acc.y *= inv;
+        acc.z *= inv;
+        acc.w *= inv;
+        *reinterpret_cast<float4*>(res + hg * HD + d0) = acc;
       }
-      const float inv = den > 0.f ? 1.f / den : 0.f;
-      acc.x *= inv;
-      acc.y *= inv;
-      acc.z *= inv;
-      acc.w *= inv;
-      *reinterpret_cast<float4*>(res + hg * HD + d0) = acc;
-    }
+    };
+    if (C::kMaxCluster > 8 && nsplit > 8)
+      merge(std::integral_constant<int, (C::kMaxCluster > 8 ? C::kMaxCluster : 8)>{});
+    else
+      merge(std::integral_constant<int, 8>{});
     bar_consumers<NCT>();
     emit_rows<HD, NCT>(a, res, job, kvh, tid, flag);
     return;
@@ -1339,6 +1344,11 @@ static cudaError_t configure_splitkv_t(int* ctas_per_sm) {
                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(KG == 1 ? C::kSmemCluster : C::kSmem));
   if (e != cudaSuccess) return e;
+  if (KG == 1 && C::kMaxCluster > 8) {
+    e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE, KG>,
+                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
   int n = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, splitkv_kernel<HD, DT, DEVROPE, KG>,
                                                     C::kThreads, C::kSmem);
@@ -1359,7 +1369,7 @@ static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.max_splits, a.cache.hkv, min(65535, jobs - j0));
     cfg.blockDim = dim3(C::kThreads);
-    cfg.dynamicSmemBytes = a.cluster > 1 ? C::kSmemCluster : C::kSmem;
+    cfg.dynamicSmemBytes = a.cluster > 1 ? C::smem_cluster(a.cluster) : C::kSmem;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     int na = 0;

@@ -15,6 +15,14 @@ constexpr int kTile = 64;
 
 // GPUs that can share one head-sharded call.
 constexpr int kMaxRanks = 8;
+// Largest thread-block cluster of the decode kernel's split merge (its
+// gather area holds this many CTAs); above 8 the launch needs the
+// non-portable cluster size.
+#ifndef QL_MAX_CLUSTER
+#define QL_MAX_CLUSTER 16
+#endif
+constexpr int kMaxClusterCtas = QL_MAX_CLUSTER;
+static_assert(kMaxClusterCtas >= 2 && kMaxClusterCtas <= 16, "cluster size");
 
 // Head-sharded output exchange over NVLink peer memory (no collective
 // library on this path).  Rank r computes query heads [head_base,
