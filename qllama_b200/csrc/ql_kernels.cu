@@ -1201,8 +1201,9 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     return;
   }
   __threadfence();
-  // Stage every split's (m, l) once, turn them into per-split weights, then
-  // let each thread sum its outputs over the splits with independent loads.
+  // Stage every split's (m, l) once; each warp turns a head's into weights
+  // (lanes over the splits, warp reductions); then each thread sums four
+  // output columns over the splits, 16 independent loads at a time.
   float* wsm = reinterpret_cast<float*>(stages);  // [split][8] weights
   float* msm = wsm + 64 * 8;                      // [split][8] maxima
   float* dsm = msm + 64 * 8;                      // [8] 1 / sum of weights
@@ -1211,26 +1212,47 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     wsm[i] = __ldcg(&a.part_ml[((pslot + (i >> 3)) * 8 + (i & 7)) * 2 + 1]);
   }
   bar_consumers<NCT>();
-  if (tid < 8) {
-    float Mx = -CUDART_INF_F;
-    for (int s = 0; s < nsplit; ++s) Mx = fmaxf(Mx, msm[s * 8 + tid]);
-    const float Mxb = Mx == -CUDART_INF_F ? 0.f : Mx;
+  for (int h = warp; h < a.group; h += NCW) {
+    float mx = -CUDART_INF_F;
+    for (int sp = lane; sp < nsplit; sp += 32) mx = fmaxf(mx, msm[sp * 8 + h]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float mb = mx == -CUDART_INF_F ? 0.f : mx;
     float den = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float w = wsm[s * 8 + tid] * exp2f(msm[s * 8 + tid] - Mxb);
-      wsm[s * 8 + tid] = w;
+    for (int sp = lane; sp < nsplit; sp += 32) {
+      const float w = wsm[sp * 8 + h] * exp2f(msm[sp * 8 + h] - mb);
+      wsm[sp * 8 + h] = w;
       den += w;
     }
-    dsm[tid] = 1.f / den;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+    if (lane == 0) dsm[h] = den > 0.f ? 1.f / den : 0.f;
   }
   bar_consumers<NCT>();
-  for (int idx = tid; idx < a.group * HD; idx += NCT) {
-    const int hg = idx / HD, d = idx % HD;
-    const float* po = a.part_o + (pslot * 8 + hg) * HD + d;
-    float num = 0.f;
-#pragma unroll 8
-    for (int s = 0; s < nsplit; ++s) num += wsm[s * 8 + hg] * __ldcg(po + static_cast<size_t>(s) * 8 * HD);
-    res[hg * HD + d] = num * dsm[hg];
+  for (int c = tid; c < a.group * (HD / 4); c += NCT) {
+    const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
+    const float4* po = reinterpret_cast<const float4*>(a.part_o + (pslot * 8 + hg) * HD + d0);
+    constexpr int kStride = 8 * HD / 4;  // float4s from one split's rows to the next's
+    constexpr int kU = 16;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 < nsplit; s0 += kU) {
+      float4 v[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u)
+        v[u] = s0 + u < nsplit ? __ldcg(po + static_cast<size_t>(s0 + u) * kStride)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const float w = s0 + u < nsplit ? wsm[(s0 + u) * 8 + hg] : 0.f;
+        acc.x = fmaf(v[u].x, w, acc.x);
+        acc.y = fmaf(v[u].y, w, acc.y);
+        acc.z = fmaf(v[u].z, w, acc.z);
+        acc.w = fmaf(v[u].w, w, acc.w);
+      }
+    }
+    const float inv = dsm[hg];
+    *reinterpret_cast<float4*>(res + hg * HD + d0) =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
   }
   if (tid == 0) a.counters[static_cast<size_t>(job) * hkv + kvh] = 0;
   bar_consumers<NCT>();
