@@ -107,6 +107,12 @@ CASES = [
     ("bf16", "bf16", 64, 16, 4, [3, 333]),
     ("q8_0", "f16", 128, 64, 8, [1, 64, 1000, 3000]),
     ("q8_0", "bf16", 128, 16, 16, [17, 900]),
+    # one sequence: a cluster of one-tile CTAs (more than 8, merged 16 wide)
+    ("f16", "f16", 64, 32, 4, [700]),
+    # one long sequence: clustered CTAs of several tiles (next tile's QK^T issued early)
+    ("bf16", "bf16", 64, 32, 4, [4000]),
+    # few long sequences at head_dim 128: the wide kernel (two groups per CTA)
+    ("f16", "f16", 128, 32, 8, [6000, 5000]),
 ]
 
 
