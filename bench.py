@@ -25,7 +25,8 @@ step are captured once into CUDA graphs and replayed, the L2 flushed between
 steps (outside the timed events).  e2e repeats the step through the C ABI from
 a native loop (qlb_run_job: one ql_attn_forward per layer per token step),
 with the step's Q/K/V copied from pinned host memory and its outputs copied
-back inside the timed region.  Multi-GPU (torchrun): every rank runs its own
+back inside the timed region (on a copy stream, in chunks of layers or token
+steps that overlap the calls).  Multi-GPU (torchrun): every rank runs its own
 replica (weak scaling, no data-path collective); times are the max over ranks.
 --impl reference times the CPU oracle (the restatement of the reference's Rust
 CPU attention) on this host's cores on a bounded sample of the same workload.
@@ -260,7 +261,7 @@ def run_ours(args, w):
     blib = ctypes.CDLL(qb.build.BENCH_LIB)
     vp, i32 = ctypes.c_void_p, ctypes.c_int32
     blib.qlb_run_job.argtypes = [vp, vp, i32, i32, i32, i32, vp, i32, i32, i32, ctypes.c_float,
-                                 i32, i32] + [vp] * 8 + [vp, i32]
+                                 i32, i32] + [vp] * 8 + [vp, i32, i32]
     blib.qlb_run_job.restype = ctypes.c_int
 
     kind = w["kind"]
@@ -316,7 +317,7 @@ def run_ours(args, w):
         ptrs = [t.data_ptr() if t.numel() else None for t in bufs]
         rc = blib.qlb_run_job(ctx._h, kv._h, Lyr, B, prefill, steps, st.ctypes.data, hq_r, hkv_r,
                               hd, w["theta"], code[w["in_dtype"]], code[w["out_dtype"]], *ptrs,
-                              comm._h if comm else None, hq)
+                              comm._h if comm else None, hq, 0)
         if rc != 0:
             raise qb.QllamaError(rc, qb.load().ql_last_error().decode())
 
@@ -408,27 +409,94 @@ def run_ours(args, w):
     value = (tok_mult if kind == "job" else world) * args.steps * step_value / t_tot
 
     # ---- e2e through the C ABI from pinned host memory
+    # The step's inputs come from pinned host memory and its outputs go back
+    # to it, every step, inside the timed region.  The copies run on a copy
+    # stream in chunks (the prefill inputs a few layers at a time, then the
+    # decode inputs a few token steps at a time) so that they overlap the
+    # calls, which wait for their chunk's inputs; each chunk's outputs are
+    # copied back once its calls end.
     host_in = [t.cpu().pin_memory() for t in (pq, pk, pv, dq, dk, dv)]
     host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (pout, dout)]
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = sum(t.numel() * t.element_size() for t in host_out)
     e2e_reps = max(1, min(args.steps, 3))
+    cstream = torch.cuda.Stream(device=dev)
+    chunk = max(1, (D + 7) // 8)  # decode steps per copy chunk
+    dchunks = [(c0, min(D, c0 + chunk)) for c0 in range(0, D, chunk)]
+    lchunk = max(1, (Lyr + 7) // 8)  # prefill layers per copy chunk
+    pchunks = [(c0, min(Lyr, c0 + lchunk)) for c0 in range(0, Lyr, lchunk)] if P else []
+
+    def job_steps(s0, s1):
+        """Decode steps [s0, s1) through the C ABI (inputs and outputs of those steps)."""
+        st = np.ascontiguousarray(lens0 + P + s0, dtype=np.int64)
+        ptrs = [None] * 4 + [t[s0].data_ptr() for t in (dq, dk, dv, dout)]
+        rc = blib.qlb_run_job(ctx._h, kv._h, Lyr, B, 0, s1 - s0, st.ctypes.data, hq_r, hkv_r, hd,
+                              w["theta"], code[w["in_dtype"]], code[w["out_dtype"]], *ptrs,
+                              comm._h if comm else None, hq, 0)
+        if rc != 0:
+            raise qb.QllamaError(rc, qb.load().ql_last_error().decode())
+
+    def job_layers(l0, l1):
+        """The prefill of cache layers [l0, l1) through the C ABI."""
+        st = np.ascontiguousarray(lens0 + P, dtype=np.int64)
+        ptrs = [t[l0].data_ptr() for t in (pq, pk, pv, pout)] + [None] * 4
+        rc = blib.qlb_run_job(ctx._h, kv._h, l1 - l0, B, P, 0, st.ctypes.data, hq_r, hkv_r, hd,
+                              w["theta"], code[w["in_dtype"]], code[w["out_dtype"]], *ptrs,
+                              comm._h if comm else None, hq, l0)
+        if rc != 0:
+            raise qb.QllamaError(rc, qb.load().ql_last_error().decode())
+
+    def e2e_step():
+        """One step: chunked copies in on `cstream`, the calls on `stream`, copies out."""
+        ev_c = torch.cuda.Event()
+        ev_c.record(stream)
+        cstream.wait_event(ev_c)  # the previous step's calls are done with the buffers
+        ready = []
+        with torch.cuda.stream(cstream):
+            for l0, l1 in pchunks:
+                for dst, src in zip((pq, pk, pv), host_in[:3]):
+                    dst[l0:l1].copy_(src[l0:l1], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(cstream)
+                ready.append(e)
+            for s0, s1 in dchunks:
+                for dst, src in zip((dq, dk, dv), host_in[3:]):
+                    dst[s0:s1].copy_(src[s0:s1], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(cstream)
+                ready.append(e)
+        with torch.cuda.stream(stream):
+            rewind()
+            k = 0
+            for l0, l1 in pchunks:
+                stream.wait_event(ready[k])
+                k += 1
+                job_layers(l0, l1)
+                e = torch.cuda.Event()
+                e.record(stream)
+                cstream.wait_event(e)
+                with torch.cuda.stream(cstream):
+                    host_out[0][l0:l1].copy_(pout[l0:l1], non_blocking=True)
+            for s0, s1 in dchunks:
+                stream.wait_event(ready[k])
+                k += 1
+                job_steps(s0, s1)
+                e = torch.cuda.Event()
+                e.record(stream)
+                cstream.wait_event(e)
+                with torch.cuda.stream(cstream):
+                    host_out[1][s0:s1].copy_(dout[s0:s1], non_blocking=True)
+        done = torch.cuda.Event()
+        done.record(cstream)
+        stream.wait_event(done)  # the step ends when its outputs are in host memory
+
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     for it in range(1 + e2e_reps):
         if it == 1:
             barrier()
             t0.record(stream)
-        rewind()
-        with torch.cuda.stream(stream):
-            for dst, src in zip((pq, pk, pv, dq, dk, dv), host_in):
-                if src.numel():
-                    dst.copy_(src, non_blocking=True)
-            for _, fn in phases:
-                fn()
-            for dst, src in zip(host_out, (pout, dout)):
-                if src.numel():
-                    dst.copy_(src, non_blocking=True)
+        e2e_step()
     t1.record(stream)
     barrier()
     ctx.synchronize()

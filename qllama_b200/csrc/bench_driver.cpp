@@ -8,7 +8,7 @@
 // tokens, sequence b from position decode_starts[b] on (either phase may be
 // empty).  With a communicator, every call is ql_attn_forward_sharded: hq and
 // hkv are this rank's heads and the outputs hold out_heads (all ranks' query
-// heads) per row.
+// heads) per row.  The calls go to cache layers layer0 .. layer0+layers-1.
 // Buffers are device pointers laid out as
 //   prefill q/k/v: [layers][batch][prefill][heads][hd]
 //   decode  q/k/v: [steps][layers][batch][1][heads][hd]
@@ -27,7 +27,7 @@ extern "C" int qlb_run_job(ql_ctx* ctx, ql_kv* kv, int32_t layers, int32_t batch
                            float theta, int32_t in_dtype, int32_t out_dtype, const void* pq,
                            const void* pk, const void* pv, void* pout, const void* dq,
                            const void* dk, const void* dv, void* dout, ql_comm* comm,
-                           int32_t out_heads) {
+                           int32_t out_heads, int32_t layer0) {
   auto call = [&](const ql_attn_args* a) {
     return comm ? ql_attn_forward_sharded(ctx, kv, comm, a) : ql_attn_forward(ctx, kv, a);
   };
@@ -54,7 +54,7 @@ extern "C" int qlb_run_job(ql_ctx* ctx, ql_kv* kv, int32_t layers, int32_t batch
     const size_t qs = (size_t)batch * prefill * hq * hd, ks = (size_t)batch * prefill * hkv * hd;
     const size_t os = (size_t)batch * prefill * out_heads * hd;
     for (int l = 0; l < layers; ++l) {
-      a.layer_idx = l;
+      a.layer_idx = layer0 + l;
       a.q = at(pq, l * qs * in_b);
       a.k = at(pk, l * ks * in_b);
       a.v = at(pv, l * ks * in_b);
@@ -70,7 +70,7 @@ extern "C" int qlb_run_job(ql_ctx* ctx, ql_kv* kv, int32_t layers, int32_t batch
   for (int s = 0; s < steps; ++s) {
     for (int l = 0; l < layers; ++l) {
       const size_t i = (size_t)s * layers + l;
-      a.layer_idx = l;
+      a.layer_idx = layer0 + l;
       a.q = at(dq, i * qs * in_b);
       a.k = at(dk, i * ks * in_b);
       a.v = at(dv, i * ks * in_b);
