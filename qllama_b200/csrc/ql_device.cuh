@@ -138,6 +138,17 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity
   return false;
 }
 
+// Atomic add at GPU scope with acquire and release semantics; returns the
+// old value.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;"
+               : "=r"(old)
+               : "l"(reinterpret_cast<uint64_t>(p)), "r"(v)
+               : "memory");
+  return old;
+}
+
 // ------------------------------------------- programmatic dependent launch --
 // Waits until the grids this one depends on have completed and their memory
 // is visible (a no-op when the launch carried no programmatic dependency).

@@ -320,7 +320,6 @@ struct SplitCfg {
                     kStages * kStageBytes,
                 "merge buffer must fit the stages");
   static_assert(KG == 1 || (!kQ8 && kStages >= KG), "wide variant: f16/bf16, a stage per group");
-  static_assert((2 * 64 * 8 + 8) * 4 <= kStages * kStageBytes, "split tables must fit the stages");
   // Q8_0 int8 q fragments [HD/32][32][4 words], per-head factors [8] and
   // half-row maxima [8][HD/64] in the q tile's space
   static_assert(!kQ8 || (HD / 32) * 512 + (8 + 8 * (HD / 64)) * 4 <= 16 * kQLd * 2,
@@ -1189,10 +1188,13 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     return;
   }
   // ---- the last CTA of this (job, kv head) merges the splits
-  __threadfence();
+  // The barrier orders every thread's partial rows before thread 0's count,
+  // whose release makes them visible at GPU scope; its acquire makes the
+  // other splits' rows visible to the last CTA, whose threads the second
+  // barrier orders after it.
   bar_consumers<NCT>();
   if (tid == 0) {
-    const int prev = atomicAdd(&a.counters[static_cast<size_t>(job) * hkv + kvh], 1);
+    const int prev = atom_add_acq_rel_gpu(&a.counters[static_cast<size_t>(job) * hkv + kvh], 1);
     flag[0] = prev == nsplit - 1;
   }
   bar_consumers<NCT>();
@@ -1200,57 +1202,49 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     if (a.peer.nranks && tid == 0) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
     return;
   }
-  __threadfence();
-  // Stage every split's (m, l) once; each warp turns a head's into weights
-  // (lanes over the splits, warp reductions); then each thread sums four
-  // output columns over the splits, 16 independent loads at a time.
-  float* wsm = reinterpret_cast<float*>(stages);  // [split][8] weights
-  float* msm = wsm + 64 * 8;                      // [split][8] maxima
-  float* dsm = msm + 64 * 8;                      // [8] 1 / sum of weights
-  for (int i = tid; i < nsplit * 8; i += NCT) {
-    msm[i] = __ldcg(&a.part_ml[((pslot + (i >> 3)) * 8 + (i & 7)) * 2]);
-    wsm[i] = __ldcg(&a.part_ml[((pslot + (i >> 3)) * 8 + (i & 7)) * 2 + 1]);
-  }
-  bar_consumers<NCT>();
-  for (int h = warp; h < a.group; h += NCW) {
-    float mx = -CUDART_INF_F;
-    for (int sp = lane; sp < nsplit; sp += 32) mx = fmaxf(mx, msm[sp * 8 + h]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float mb = mx == -CUDART_INF_F ? 0.f : mx;
-    float den = 0.f;
-    for (int sp = lane; sp < nsplit; sp += 32) {
-      const float w = wsm[sp * 8 + h] * exp2f(msm[sp * 8 + h] - mb);
-      wsm[sp * 8 + h] = w;
-      den += w;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-    if (lane == 0) dsm[h] = den > 0.f ? 1.f / den : 0.f;
-  }
-  bar_consumers<NCT>();
+  // Each thread sums four output columns over the splits with a running
+  // maximum, loading kU splits' (max, sum) and rows at a time: one round
+  // trip to L2 per kU splits.
   for (int c = tid; c < a.group * (HD / 4); c += NCT) {
     const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
     const float4* po = reinterpret_cast<const float4*>(a.part_o + (pslot * 8 + hg) * HD + d0);
+    const float2* pm = reinterpret_cast<const float2*>(a.part_ml + (pslot * 8 + hg) * 2);
     constexpr int kStride = 8 * HD / 4;  // float4s from one split's rows to the next's
-    constexpr int kU = 16;
+    constexpr int kU = KG > 2 ? 4 : 16;  // the four-group variant has 96 registers
+    float M = -CUDART_INF_F, den = 0.f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int s0 = 0; s0 < nsplit; s0 += kU) {
       float4 v[kU];
-#pragma unroll
-      for (int u = 0; u < kU; ++u)
-        v[u] = s0 + u < nsplit ? __ldcg(po + static_cast<size_t>(s0 + u) * kStride)
-                               : make_float4(0.f, 0.f, 0.f, 0.f);
+      float2 ml[kU];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
-        const float w = s0 + u < nsplit ? wsm[(s0 + u) * 8 + hg] : 0.f;
+        const bool live = s0 + u < nsplit;
+        v[u] = live ? __ldcg(po + static_cast<size_t>(s0 + u) * kStride)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+        ml[u] = live ? __ldcg(pm + static_cast<size_t>(s0 + u) * 8) : make_float2(-CUDART_INF_F, 0.f);
+      }
+      float cm = M;
+#pragma unroll
+      for (int u = 0; u < kU; ++u) cm = fmaxf(cm, ml[u].x);
+      const float cb = cm == -CUDART_INF_F ? 0.f : cm;
+      const float r = M == -CUDART_INF_F ? 0.f : exp2f(M - cb);  // rescale what came before
+      acc.x *= r;
+      acc.y *= r;
+      acc.z *= r;
+      acc.w *= r;
+      den *= r;
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const float w = ml[u].y * exp2f(ml[u].x - cb);  // 0 past the live splits
+        den += w;
         acc.x = fmaf(v[u].x, w, acc.x);
         acc.y = fmaf(v[u].y, w, acc.y);
         acc.z = fmaf(v[u].z, w, acc.z);
         acc.w = fmaf(v[u].w, w, acc.w);
       }
+      M = cm;
     }
-    const float inv = dsm[hg];
+    const float inv = den > 0.f ? 1.f / den : 0.f;
     *reinterpret_cast<float4*>(res + hg * HD + d0) =
         make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
   }
