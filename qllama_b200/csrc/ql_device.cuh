@@ -114,6 +114,15 @@ __device__ __forceinline__ void st_async_v4(uint32_t remote_addr, const float4& 
       "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(remote_bar)
       : "memory");
 }
+// The 8-byte form of st_async_v4.
+__device__ __forceinline__ void st_async_v2(uint32_t remote_addr, const float2& v,
+                                            uint32_t remote_bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+          remote_addr),
+      "f"(v.x), "f"(v.y), "r"(remote_bar)
+      : "memory");
+}
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity,
                                                   uint32_t* status) {
   auto try_wait = [&]() {
@@ -328,6 +337,25 @@ __device__ __forceinline__ void store8(void* base, size_t i, int dt, const float
   for (int e = 0; e < 4; ++e)
     w[e] = dt == kF16 ? pack2<false>(x[2 * e], x[2 * e + 1]) : pack2<true>(x[2 * e], x[2 * e + 1]);
   *reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + i) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Four consecutive output elements (i a multiple of 4) in one store when
+// `vec` says the base is 16-byte aligned.
+__device__ __forceinline__ void store4(void* base, size_t i, int dt, const float4& x, bool vec) {
+  if (!vec) {
+    store_elem(base, i, dt, x.x);
+    store_elem(base, i + 1, dt, x.y);
+    store_elem(base, i + 2, dt, x.z);
+    store_elem(base, i + 3, dt, x.w);
+    return;
+  }
+  if (dt == kF32) {
+    *reinterpret_cast<float4*>(static_cast<float*>(base) + i) = x;
+    return;
+  }
+  const uint32_t w0 = dt == kF16 ? pack2<false>(x.x, x.y) : pack2<true>(x.x, x.y);
+  const uint32_t w1 = dt == kF16 ? pack2<false>(x.z, x.w) : pack2<true>(x.z, x.w);
+  *reinterpret_cast<uint2*>(static_cast<uint16_t*>(base) + i) = make_uint2(w0, w1);
 }
 
 // ------------------------------------------- flags shared between GPUs --

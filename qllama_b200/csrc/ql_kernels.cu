@@ -1074,6 +1074,17 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   bar_consumers<NCT>();
   const int tid = threadIdx.x;
   const size_t pslot = (static_cast<size_t>(job) * hkv + kvh) * a.max_splits;
+  // Cluster mode: every split but rank 0 sends its rows and (max, sum) per
+  // head straight from the merge below into rank 0's shared memory, by
+  // asynchronous remote stores that count their bytes on rank 0's mbarrier.
+  const bool sender = cl && split != 0;
+  uint32_t rbar = 0, drow = 0, dml = 0;
+  if (sender) {
+    cluster_wait();  // rank 0's mbarrier is initialised
+    rbar = mapa_shared(smem_u32(gbar), 0);
+    drow = mapa_shared(smem_u32(grows + split * 8 * HD), 0);
+    dml = mapa_shared(smem_u32(gml + split * 16), 0);
+  }
   // Each thread forms its head's weights itself (a few exponentials, no
   // serial step and no barrier) and sums four columns over the warps.
   for (int c = tid; c < a.group * (HD / 4); c += NCT) {
@@ -1099,7 +1110,10 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     acc.y *= inv;
     acc.z *= inv;
     acc.w *= inv;
-    if (nsplit == 1 || cl) {
+    if (sender) {
+      st_async_v4(drow + 4 * (hg * HD + d0), acc, rbar);
+      if (d0 == 0) st_async_v2(dml + 8 * hg, make_float2(M, Lh), rbar);
+    } else if (nsplit == 1 || cl) {
       *reinterpret_cast<float4*>(res + hg * HD + d0) = acc;
       if (d0 == 0) {
         cml[2 * hg] = M;
@@ -1114,28 +1128,21 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     }
   }
   if (cl) {
-    // Rows of split r travel to rank 0 by asynchronous remote stores that
-    // count their bytes on rank 0's mbarrier; rank 0 expects the bytes of
-    // every live split but itself.
-    constexpr uint32_t kPushRow = HD * 4;
-    const uint32_t push_bytes = a.group * kPushRow + 16 * 4;
-    bar_consumers<NCT>();  // res and cml are complete
-    if (split != 0) {
-      cluster_wait();  // rank 0's mbarrier is initialised
-      const uint32_t rbar = mapa_shared(smem_u32(gbar), 0);
-      const uint32_t drow = mapa_shared(smem_u32(grows + split * 8 * HD), 0);
-      const uint32_t dml = mapa_shared(smem_u32(gml + split * 16), 0);
-      for (int i = tid; i < a.group * HD / 4; i += NCT)
-        st_async_v4(drow + 16 * i, reinterpret_cast<const float4*>(res)[i], rbar);
-      if (tid < 4) st_async_v4(dml + 16 * tid, reinterpret_cast<const float4*>(cml)[tid], rbar);
+    if (sender) {
       if (tid == 0 && a.peer.nranks) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
       return;
     }
-    // Rank 0: the other splits' rows have landed (bounded wait, acquire at
-    // cluster scope); merge the live splits by LSE weight, each thread
-    // forming its head's weights.
+    // Rank 0 expects the bytes of every live split but itself (rows and
+    // (max, sum) of the group's heads); once they have landed (bounded wait,
+    // acquire at cluster scope) it merges the live splits by LSE weight, each
+    // thread forming its head's weights, and stores its four columns.
+    const uint32_t push_bytes = a.group * (HD * 4 + 8);
+    bar_consumers<NCT>();  // its own res and cml are complete
     if (tid == 0) mbar_arrive_expect_tx(gbar, (nsplit - 1) * push_bytes);
     mbar_wait_cluster(gbar, 0, a.status);
+    // A single GPU's output is stored from registers; a head-sharded call's
+    // goes through emit_rows, which writes every rank's buffer in protocol.
+    const bool direct = a.peer.nranks == 0;
     // Unrolled over 8 or over the largest cluster with predicated loads, so
     // that all the loads issue at once; splits past nsplit weigh 0.
     auto merge = [&](auto width) {
@@ -1171,15 +1178,21 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
         acc.y *= inv;
         acc.z *= inv;
         acc.w *= inv;
-        *reinterpret_cast<float4*>(res + hg * HD + d0) = acc;
+        if (direct)
+          store4(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d0,
+                 a.out_dtype, acc, a.out_vec != 0);
+        else
+          *reinterpret_cast<float4*>(res + hg * HD + d0) = acc;
       }
     };
     if (C::kMaxCluster > 8 && nsplit > 8)
       merge(std::integral_constant<int, (C::kMaxCluster > 8 ? C::kMaxCluster : 8)>{});
     else
       merge(std::integral_constant<int, 8>{});
-    bar_consumers<NCT>();
-    emit_rows<HD, NCT>(a, res, job, kvh, tid, flag);
+    if (!direct) {
+      bar_consumers<NCT>();
+      emit_rows<HD, NCT>(a, res, job, kvh, tid, flag);
+    }
     return;
   }
   if (nsplit == 1) {
