@@ -113,6 +113,10 @@ struct ql_kv {
   std::vector<int64_t> len;            // [layer][seq] written prefix
   double2* d_rope = nullptr;           // [max_seq_len][head_dim/2] (cos, sin)
   float rope_theta = 0.f;
+  // Duplicate-sequence check of a call without per-call allocation: slot s
+  // was named by the current call when seen_mark[s] == seen_epoch.
+  std::vector<uint32_t> seen_mark;
+  uint32_t seen_epoch = 0;
 };
 
 namespace {
@@ -221,11 +225,11 @@ int ensure_rope(ql_kv* kv, float theta) {
 
 // Gives every listed sequence the pages its new length needs; rolls back on
 // exhaustion so that the call stays transactional.
-int reserve_pages(ql_kv* kv, const std::vector<int32_t>& seqs, const std::vector<int64_t>& ends) {
+int reserve_pages(ql_kv* kv, const int32_t* seqs, const int64_t* ends, int count) {
   const int P = kv->cfg.page_size, pps = kv->pages_per_seq;
-  std::vector<std::pair<int, int>> taken;  // (seq, logical page)
+  std::vector<std::pair<int, int>> taken;  // (seq, logical page); grows only with new pages
   bool changed = false;
-  for (size_t i = 0; i < seqs.size(); ++i) {
+  for (int i = 0; i < count; ++i) {
     const int s = seqs[i];
     const int need = static_cast<int>((ends[i] + P - 1) / P);
     while (kv->seq_pages[s] < need) {
@@ -253,6 +257,16 @@ int reserve_pages(ql_kv* kv, const std::vector<int32_t>& seqs, const std::vector
             "upload block table");
   }
   return QL_OK;
+}
+
+// A fresh mark for the duplicate check of one call (the marks are cleared
+// when the counter wraps).
+uint32_t next_seen_epoch(ql_kv* kv) {
+  if (++kv->seen_epoch == 0) {
+    std::fill(kv->seen_mark.begin(), kv->seen_mark.end(), 0u);
+    kv->seen_epoch = 1;
+  }
+  return kv->seen_epoch;
 }
 
 int64_t& len_at(ql_kv* kv, int layer, int seq) {
@@ -293,15 +307,16 @@ struct SplitPlan {
 //    lost.  While it would leave more than a tenth of them idle, up to four
 //    times as many splits are tried; the first that fills 90% is kept, else
 //    the fullest.
-SplitPlan plan_splits(const std::vector<int>& tiles, long long per_row, long long slots) {
+SplitPlan plan_splits(const int* tiles, int rows, long long per_row, long long slots) {
   constexpr int kMinSplitTiles = 16, kMaxSplits = 64;
   int max_tiles = 1;
   long long total = 0;
-  for (int t : tiles) {
+  for (int r = 0; r < rows; ++r) {
+    const int t = tiles[r];
     max_tiles = std::max(max_tiles, t);
     total += t * per_row;
   }
-  const long long jobs = per_row * static_cast<long long>(tiles.size());
+  const long long jobs = per_row * static_cast<long long>(rows);
   slots = std::max(1LL, slots);
   int tps = max_tiles;
   if (jobs < 2 * slots) {
@@ -313,7 +328,7 @@ SplitPlan plan_splits(const std::vector<int>& tiles, long long per_row, long lon
   tps = (max_tiles + splits - 1) / splits;
   auto fill = [&](int t) {
     long long ctas = 0;
-    for (int x : tiles) ctas += (x + t - 1) / t * per_row;
+    for (int r = 0; r < rows; ++r) ctas += (tiles[r] + t - 1) / t * per_row;
     const long long waves = (ctas + slots - 1) / slots;
     return static_cast<double>(ctas) / static_cast<double>(waves * slots);
   };
@@ -500,6 +515,7 @@ int ql_kv_create(ql_ctx* c, const ql_kv_config* cfg_in, ql_kv** out) {
   }
   kv->table.assign(static_cast<size_t>(cfg.max_batch) * std::max(1, kv->pages_per_seq), -1);
   kv->seq_pages.assign(cfg.max_batch, 0);
+  kv->seen_mark.assign(cfg.max_batch, 0);
   for (int p = cfg.num_pages - 1; p >= 0; --p) kv->free_pages.push_back(p);
   kv->len.assign(static_cast<size_t>(std::max(1, cfg.num_layers)) * cfg.max_batch, 0);
   cudaError_t e = cudaMalloc(&kv->d_table, kv->table.size() * sizeof(int32_t));
@@ -638,7 +654,9 @@ int ql_kv_update(ql_ctx* c, ql_kv* kv, int32_t layer, int32_t seq, const void* k
   if (n == 0) return QL_OK;  // empty batch: no-op (cache.rs:77-78)
   if (n > INT32_MAX / (hkv * 32)) return fail(QL_ERR_INVALID, "batch too large");
   QL_CUDA(cudaSetDevice(c->device), "set device");
-  int r = reserve_pages(kv, {seq}, {cur + n});
+  const int32_t one_seq = seq;
+  const int64_t one_end = cur + n;
+  int r = reserve_pages(kv, &one_seq, &one_end, 1);
   if (r != QL_OK) return r;
   const size_t in_bytes = static_cast<size_t>(n) * hkv * hd * elem_bytes(in_dtype);
   const void *kd_ptr = k, *vd_ptr = v;
@@ -750,16 +768,17 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
   if (hkv != kv->cfg.num_kv_heads || hd != kv->cfg.head_dim)
     return fail(QL_ERR_INVALID, "K shape [%d, %d, %d] does not match cache [_, %d, %d]", n, hkv,
                 hd, kv->cfg.num_kv_heads, kv->cfg.head_dim);
-  std::vector<int32_t> seqs(a->batch);
-  std::vector<int64_t> ends(a->batch);
-  std::vector<char> seen(kv->cfg.max_batch, 0);
+  int32_t seqs[ql::kMaxBatch];
+  int64_t ends[ql::kMaxBatch];
+  const uint32_t mark = next_seen_epoch(kv);
   for (int b = 0; b < a->batch; ++b) {
     const int s = a->seq_ids[b];
     if (s < 0 || s >= kv->cfg.max_batch)
       return fail(QL_ERR_INVALID, "sequence %d out of range (cache has %d slots)", s,
                   kv->cfg.max_batch);
-    if (seen[s]) return fail(QL_ERR_INVALID, "sequence %d appears twice in one call", s);
-    seen[s] = 1;
+    if (kv->seen_mark[s] == mark)
+      return fail(QL_ERR_INVALID, "sequence %d appears twice in one call", s);
+    kv->seen_mark[s] = mark;
     const int64_t start = a->start_pos[b];
     if (start < 0) return fail(QL_ERR_INVALID, "start_pos %lld is negative", (long long)start);
     const int64_t last = start + (n > 0 ? n - 1 : 0);
@@ -792,7 +811,7 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
     return fail(QL_ERR_UNSUPPORTED, "the fused head-sharded exchange needs a single-token "
                 "decode on the split-KV kernel");
   QL_CUDA(cudaSetDevice(c->device), "set device");
-  int r = reserve_pages(kv, seqs, ends);
+  int r = reserve_pages(kv, seqs, ends, a->batch);
   if (r != QL_OK) return r;
   r = ensure_rope(kv, a->rope_theta);
   if (r != QL_OK) return r;
@@ -808,7 +827,7 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
   // split planning for the tensor-core kernel
   int max_tiles = 0;
   int max_len = 0;
-  std::vector<int> row_tiles(a->batch);
+  int row_tiles[ql::kMaxBatch];
   for (int b = 0; b < a->batch; ++b) {
     const int64_t end = ends[b];
     max_len = std::max<int>(max_len, static_cast<int>(end));
@@ -848,7 +867,8 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
   } else if (fast) {
     const int per_sm = std::max(1, ql::splitkv_ctas_per_sm(hd, kv->cfg.dtype, false));
     const SplitPlan plan =
-        plan_splits(row_tiles, static_cast<long long>(n) * hkv, 1LL * per_sm * c->num_sms);
+        plan_splits(row_tiles, a->batch, static_cast<long long>(n) * hkv,
+                    1LL * per_sm * c->num_sms);
     tps = plan.tps;
     max_splits = plan.splits;
   }
@@ -1032,18 +1052,19 @@ int ql_attn_decode_noalloc(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
     return fail(QL_ERR_UNSUPPORTED, "ql_attn_decode_noalloc needs an f16/bf16 cache with head_dim "
                 "64 or 128 or a Q8_0 cache with head_dim 128, and at most 8 query heads per KV "
                 "head");
-  std::vector<int32_t> seqs(a->batch);
-  std::vector<int64_t> ends(a->batch);
-  std::vector<char> seen(kv->cfg.max_batch, 0);
+  int32_t seqs[ql::kMaxBatch];
+  int64_t ends[ql::kMaxBatch];
   int max_tiles = 0;
-  std::vector<int> row_tiles(a->batch);
+  int row_tiles[ql::kMaxBatch];
+  const uint32_t mark = next_seen_epoch(kv);
   for (int b = 0; b < a->batch; ++b) {
     const int s = a->seq_ids[b];
     if (s < 0 || s >= kv->cfg.max_batch)
       return fail(QL_ERR_INVALID, "sequence %d out of range (cache has %d slots)", s,
                   kv->cfg.max_batch);
-    if (seen[s]) return fail(QL_ERR_INVALID, "sequence %d appears twice in one call", s);
-    seen[s] = 1;
+    if (kv->seen_mark[s] == mark)
+      return fail(QL_ERR_INVALID, "sequence %d appears twice in one call", s);
+    kv->seen_mark[s] = mark;
     const int64_t start = a->start_pos[b], cur = len_at(kv, layer, s);
     if (start < 0) return fail(QL_ERR_INVALID, "start_pos %lld is negative", (long long)start);
     if (start != cur)
@@ -1063,12 +1084,12 @@ int ql_attn_decode_noalloc(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   char* scratch = nullptr;
   int r = noalloc_scratch(c->device, &scratch);
   if (r != QL_OK) return r;
-  r = reserve_pages(kv, seqs, ends);  // hands out pool pages; allocates nothing
+  r = reserve_pages(kv, seqs, ends, a->batch);  // hands out pool pages; allocates nothing
   if (r != QL_OK) return r;
   // Split plan of ql_attn_forward, with fewer splits if the partials would not fit.
   const int jobs = a->batch;
   const int per_sm = std::max(1, ql::splitkv_ctas_per_sm(hd, kv->cfg.dtype, true));
-  int tps = plan_splits(row_tiles, hkv, 1LL * per_sm * c->num_sms).tps;
+  int tps = plan_splits(row_tiles, a->batch, hkv, 1LL * per_sm * c->num_sms).tps;
   auto part_bytes = [&](int splits) {
     return align256(static_cast<size_t>(jobs) * hkv * splits * 8 * 2 * sizeof(float)) +
            static_cast<size_t>(jobs) * hkv * splits * 8 * hd * sizeof(float);

@@ -237,6 +237,14 @@ def test_operator_errors_are_transactional(ctx):
     assert c.seq_len() == 126
     e = qb.attention_forward(c, 0, q[:, :0], k[:, :0], v[:, :0], [126], hq, hkv, hd, theta)
     assert tuple(e.shape) == (1, 0, hq * hd) and c.seq_len() == 126
+    # a sequence named twice in one call is rejected, and the next calls that
+    # name each sequence once go through
+    q2, k2, v2 = (gu.to_device(gu.normal(rng, (2, 1, h, hd)), "f16") for h in (hq, hkv, hkv))
+    with pytest.raises(qb.QllamaError, match="appears twice"):
+        qb.attention_forward(c, 1, q2, k2, v2, [0, 0], hq, hkv, hd, theta, seq_ids=[1, 1])
+    for pos in range(2):
+        qb.attention_forward(c, 1, q2, k2, v2, [pos, pos], hq, hkv, hd, theta, seq_ids=[1, 0])
+    assert c.layer_len(1, 1) == 2 and c.layer_len(1, 0) == 2
 
 
 def test_tiny_llama_end_to_end_on_gpu(ctx, golden):
