@@ -2,7 +2,7 @@
 """Benchmark of the Qllama attention hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload c2|c3|c4|c5]
+                    [--workload c2|c3|c4|c5] [--only]
 
 Workloads (seeded synthetic N(0,1) inputs of the named shapes; cache contents
 random where the shape says "pre-filled"):
@@ -20,14 +20,28 @@ random where the shape says "pre-filled"):
   c5 Llama-3-70B-shaped GQA decode: 64/8 heads, head_dim 128, Q8_0 KV of
      length 32768, 64 sequences; a step is 16 decode steps of one layer (80
      layers do not fit one GPU).  value: KV GB/s.
+
+The line's headline is the chosen workload (c2 by default).  Unless --only is
+given, the same run also measures the other workloads and reports them under
+"workloads": on one GPU c3, c4 and c5 (fewer timed steps, stated per entry);
+under torchrun the 70B-shaped decode with its KV heads split over the GPUs,
+once with the exchange fused into the decode kernel (NVLink peer stores) and
+once with the NCCL all-gather baseline, after a check of the sharded output
+against a single-GPU call over all heads on rank 0.
+
 value is measured with the inputs resident in HBM: the API's launches for a
 step are captured once into CUDA graphs and replayed, the L2 flushed between
 steps (outside the timed events).  e2e repeats the step through the C ABI from
 a native loop (qlb_run_job: one ql_attn_forward per layer per token step),
 with the step's Q/K/V copied from pinned host memory and its outputs copied
-back inside the timed region (on a copy stream, in chunks of layers or token
-steps that overlap the calls).  Multi-GPU (torchrun): every rank runs its own
-replica (weak scaling, no data-path collective); times are the max over ranks.
+back inside the timed region (on a copy stream, in chunks that overlap the
+calls).  The e2e steps also pay for page reservation: decode workloads keep
+going from where the previous step ended (sequences enter new pages as they
+grow) and whole jobs release their pages between steps (ql_kv_clear_seq).
+
+Multi-GPU (torchrun): the TinyLlama-shaped job splits its 4 KV heads over 2 or
+4 GPUs (strong scaling: outputs all-gathered over NVLink inside the kernels)
+and runs one replica per GPU on 8; times are the max over ranks.
 --impl reference times the CPU oracle (the restatement of the reference's Rust
 CPU attention) on this host's cores on a bounded sample of the same workload.
 """
@@ -54,27 +68,30 @@ WORKLOADS = {
                desc="TinyLlama-1.1B-shaped attention: 22 layers, 32 Q / 4 KV heads, head_dim 64, "
                     "theta 1e4, f16 KV, batch 1, causal prefill 512 then 256 decode steps",
                layers=22, hq=32, hkv=4, hd=64, theta=10000.0, kv="f16", batch=1, prefill=512,
-               decode=256, in_dtype="f16", out_dtype="f16", page=64),
+               decode=256, in_dtype="f16", out_dtype="f16", page=64, shard_upto=4),
     "c3": dict(kind="decode", unit="GB/s",
                desc="Llama-2-7B-shaped MHA decode: 32 layers, 32/32 heads, head_dim 128, f16 KV "
                     "pre-filled to ragged lengths U[1024,4096], batch 16, 128 decode steps",
                layers=32, hq=32, hkv=32, hd=128, theta=10000.0, kv="f16", batch=16, prefill=0,
-               len_lo=1024, len_hi=4096, decode=128, in_dtype="f16", out_dtype="f16", page=64),
+               len_lo=1024, len_hi=4096, decode=128, in_dtype="f16", out_dtype="f16", page=64,
+               shard_upto=0),
     "c4": dict(kind="prefill", unit="TFLOP/s",
                desc="Llama-3-8B-shaped GQA causal prefill: 32/8 heads, head_dim 128, theta 5e5, "
                     "bf16 Q/K/V, f16 KV, batch 4 x 8192 tokens, one layer",
                layers=1, hq=32, hkv=8, hd=128, theta=500000.0, kv="f16", batch=4, prefill=8192,
-               decode=0, in_dtype="bf16", out_dtype="bf16", page=64),
+               decode=0, in_dtype="bf16", out_dtype="bf16", page=64, shard_upto=0),
     "c5": dict(kind="decode", unit="GB/s",
                desc="Llama-3-70B-shaped GQA decode: 64/8 heads, head_dim 128, Q8_0 KV at length "
                     "32768, batch 64, one layer of 80",
                layers=1, hq=64, hkv=8, hd=128, theta=500000.0, kv="q8_0", batch=64, prefill=0,
                len_lo=32768 - 16, len_hi=32768 - 16, decode=16, in_dtype="bf16",
-               out_dtype="bf16", page=64, shard=True),
+               out_dtype="bf16", page=64, shard_upto=8),
 }
 
 KV_BYTES = {"f16": 2.0, "bf16": 2.0, "f32": 4.0, "q8_0": 34.0 / 32.0}
 IO_BYTES = {"f16": 2, "bf16": 2, "f32": 4}
+# The oracle's CPU sample of the job workload: this many of its layers, scaled.
+CPU_JOB_LAYERS = 4
 
 
 def peaks():
@@ -108,6 +125,29 @@ def seq_lengths(w, rank=0):
         return np.zeros(w["batch"], np.int64)
     rng = np.random.default_rng(4096 + rank)
     return rng.integers(w["len_lo"], w["len_hi"] + 1, size=w["batch"]).astype(np.int64)
+
+
+def sharded(w, world):
+    """Whether the workload splits its KV heads over `world` GPUs (else replicas)."""
+    return 1 < world <= w["shard_upto"] and w["hkv"] % world == 0
+
+
+def parallelism(w, world):
+    if world == 1:
+        return "1 GPU"
+    if sharded(w, world):
+        hkv_r, hq_r = w["hkv"] // world, w["hq"] // world
+        return (f"KV heads split over {world} GPUs ({hkv_r} KV / {hq_r} query heads each), "
+                f"outputs all-gathered over NVLink inside the kernels")
+    return f"{world} independent replicas, one per GPU"
+
+
+def config_of(name, w, world):
+    """The workload a line measures; both arms print the same dict."""
+    return {"workload": name, "desc": w["desc"], "layers": w["layers"], "num_heads": w["hq"],
+            "num_kv_heads": w["hkv"], "head_dim": w["hd"], "kv_dtype": w["kv"],
+            "batch": w["batch"], "prefill": w["prefill"], "decode_steps": w["decode"],
+            "page_size": w["page"], "parallelism": parallelism(w, world)}
 
 
 # ---------------------------------------------------------------- clocks ----
@@ -159,11 +199,12 @@ def _cpu_inputs(rng, m, heads, hd):
     return rng.standard_normal((m, heads, hd)).astype(np.float16).astype(np.float32)
 
 
-def cpu_sample(w, layers=None, seed=7):
+def cpu_sample(w, seed=7):
     """A bounded sample of the workload on the host through the CPU oracle.
 
     Returns the value the reference's CPU path reaches on it, in the
     workload's unit, with a description of what was run and how it scales.
+    Both arms of the benchmark report this same sample.
     """
     import oracle
 
@@ -173,7 +214,7 @@ def cpu_sample(w, layers=None, seed=7):
     hq, hkv, hd, th = w["hq"], w["hkv"], w["hd"], w["theta"]
     if w["kind"] == "job":
         P, D = w["prefill"], w["decode"]
-        n = w["layers"] if layers is None else layers
+        n = min(w["layers"], CPU_JOB_LAYERS)
         cache = oracle.KvCache(n, P + D, hkv, hd, oracle.F32)
         t = 0.0
         for layer in range(n):
@@ -221,9 +262,10 @@ def cpu_sample(w, layers=None, seed=7):
 def run_reference(args, w):
     if int(os.environ.get("RANK", "0")) != 0:
         return
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     vals, last = [], None
     for i in range(args.warmup + args.steps):
-        last = cpu_sample(w, layers=4 if w["kind"] == "job" else None, seed=100 + i)
+        last = cpu_sample(w, seed=100 + i)
         if i >= args.warmup:
             vals.append(last["value"])
     value = statistics.median(vals)
@@ -231,9 +273,10 @@ def run_reference(args, w):
     cb["value"] = value
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": w["unit"],
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": {"workload": args.workload, "desc": w["desc"]},
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": None,
+        "higher_is_better": True, "scaling": "strong" if sharded(w, world) else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_of(args.workload, w, world),
         "cpu_baseline": cb,
         "e2e": {"value": value, "unit": w["unit"], "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0}}), flush=True)
@@ -241,35 +284,97 @@ def run_reference(args, w):
 
 # ------------------------------------------------------------------ GPU -----
 
-def run_ours(args, w):
-    import torch
-    import torch.distributed as dist
+class Env:
+    """Process-wide state of one GPU rank."""
 
-    import qllama_b200 as qb
+    def __init__(self):
+        import torch
+        import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        import datetime
+        import qllama_b200 as qb
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    qb.load()
-    blib = ctypes.CDLL(qb.build.BENCH_LIB)
-    vp, i32 = ctypes.c_void_p, ctypes.c_int32
-    blib.qlb_run_job.argtypes = [vp, vp, i32, i32, i32, i32, vp, i32, i32, i32, ctypes.c_float,
-                                 i32, i32] + [vp] * 8 + [vp, i32, i32]
-    blib.qlb_run_job.restype = ctypes.c_int
+        self.torch, self.dist, self.qb = torch, dist, qb
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            import datetime
 
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=self.dev)
+        qb.load()
+        blib = ctypes.CDLL(qb.build.BENCH_LIB)
+        vp, i32 = ctypes.c_void_p, ctypes.c_int32
+        blib.qlb_run_job.argtypes = [vp, vp, i32, i32, i32, i32, vp, i32, i32, i32,
+                                     ctypes.c_float, i32, i32] + [vp] * 8 + [vp, i32, i32]
+        blib.qlb_run_job.restype = ctypes.c_int
+        self.blib = blib
+        self.ctx = qb.Context(self.local)
+        self.stream = torch.cuda.Stream(device=self.dev)
+        self.ctx.set_stream(self.stream.cuda_stream)
+        gpu_index = self.local
+        cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if cvd:
+            gpu_index = int(cvd.split(",")[self.local])
+        self.gpu_index = gpu_index
+        self.flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=self.dev)
+
+    def barrier(self):
+        self.torch.cuda.synchronize(self.dev)
+        if self.world > 1:
+            self.dist.barrier()
+        self.torch.cuda.synchronize(self.dev)
+
+    def max_over_ranks(self, values):
+        if self.world == 1:
+            return list(values)
+        t = self.torch.tensor(list(values), device=self.dev, dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return t.tolist()
+
+    def comm(self, max_bytes, mode):
+        uid = [self.qb.comm_unique_id() if self.rank == 0 else None]
+        self.dist.broadcast_object_list(uid, src=0)
+        return self.qb.Comm(self.ctx, self.world, self.rank, uid[0], max_bytes, mode)
+
+    def close(self):
+        self.ctx.close()
+        if self.world > 1:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def graph_kernel_nodes(g):
+    """Kernel launches a captured CUDA graph holds (None if it cannot be read)."""
+    try:
+        from cuda.bindings import runtime as rt
+
+        graph = rt.cudaGraph_t(init_value=g.raw_cuda_graph())
+        err, _, n = rt.cudaGraphGetNodes(graph, 0)
+        if err != rt.cudaError_t.cudaSuccess:
+            return None
+        err, nodes, n = rt.cudaGraphGetNodes(graph, n)
+        if err != rt.cudaError_t.cudaSuccess:
+            return None
+        count = 0
+        for node in nodes[:n]:
+            err, typ = rt.cudaGraphNodeGetType(node)
+            if err == rt.cudaError_t.cudaSuccess and typ == rt.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+                count += 1
+        return count
+    except Exception:  # an older cuda-python: the count is computed instead
+        return None
+
+
+def measure(env, name, w, steps, warmup, comm_mode="p2p", with_e2e=True):
+    """One workload on this rank: device-timed graph replays, then e2e."""
+    torch, qb = env.torch, env.qb
+    world, rank, dev = env.world, env.rank, env.dev
     kind = w["kind"]
     Lyr, hq, hkv, hd, B = w["layers"], w["hq"], w["hkv"], w["hd"], w["batch"]
-    # Under torchrun the 70B-shaped decode splits its KV heads over the GPUs
-    # (strong scaling, outputs all-gathered inside the decode kernel); the
-    # other workloads run one independent replica per GPU (weak scaling).
-    shard = world > 1 and (args.shard == "heads" or (args.shard == "auto" and w.get("shard")))
+    shard = sharded(w, world)
     if shard:
         qb.shard_heads(hq, hkv, world, rank)  # raises unless the heads split evenly
     hq_r, hkv_r = (hq // world, hkv // world) if shard else (hq, hkv)  # this rank's heads
@@ -279,22 +384,19 @@ def run_ours(args, w):
     code = {"f32": qb.F32, "f16": qb.F16, "bf16": qb.BF16}
     gen = torch.Generator(device=dev)
     gen.manual_seed(1234 + rank)
+    ctx, stream, blib = env.ctx, env.stream, env.blib
 
     def rnd(*shape):
         if 0 in shape:
             return torch.empty(0, device=dev, dtype=in_t)
         return torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32).to(in_t)
 
-    ctx = qb.Context(local)
-    stream = torch.cuda.Stream(device=dev)
-    ctx.set_stream(stream.cuda_stream)
+    e2e_reps = max(1, min(steps, 3))
     lens0 = seq_lengths(w, 0 if shard else rank)  # lengths before the step's first new token
-    kv = qb.KvCache(ctx, Lyr, int(lens0.max()) + P + D, hkv_r, hd, w["kv"], w["page"], B)
-    comm = None
-    if shard:
-        uid = [qb.comm_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        comm = qb.Comm(ctx, world, rank, uid[0], B * max(P, 1) * hq * hd * 4, "p2p")
+    # decode e2e steps continue past the graph-replayed step (1 untimed + e2e_reps)
+    cap = int(lens0.max()) + P + D * (2 + e2e_reps if kind == "decode" else 1)
+    kv = qb.KvCache(ctx, Lyr, cap, hkv_r, hd, w["kv"], w["page"], B)
+    comm = env.comm(B * max(P, 1) * hq * hd * 4, comm_mode) if shard else None
     if kind == "decode":  # pre-fill: seeded N(0,1) rotated keys and values
         for layer in range(Lyr):
             for b in range(B):
@@ -308,18 +410,18 @@ def run_ours(args, w):
     dk, dv = rnd(D, Lyr, B, 1, hkv_r, hd), rnd(D, Lyr, B, 1, hkv_r, hd)
     pout = torch.empty(Lyr, B, P, hq * hd, device=dev, dtype=out_t)
     dout = torch.empty(D, Lyr, B, 1, hq * hd, device=dev, dtype=out_t)
-    bufs = (pq, pk, pv, pout, dq, dk, dv, dout)
 
-    def job(prefill, steps):
-        """One phase through the C ABI: `prefill` tokens from position 0, or
-        `steps` single-token steps from each sequence's length after the prefill."""
-        st = np.ascontiguousarray(lens0 + P, dtype=np.int64)
-        ptrs = [t.data_ptr() if t.numel() else None for t in bufs]
-        rc = blib.qlb_run_job(ctx._h, kv._h, Lyr, B, prefill, steps, st.ctypes.data, hq_r, hkv_r,
-                              hd, w["theta"], code[w["in_dtype"]], code[w["out_dtype"]], *ptrs,
-                              comm._h if comm else None, hq, 0)
+    def run_job(layer0, layers, prefill, steps_, starts, ptrs):
+        st = np.ascontiguousarray(starts, dtype=np.int64)
+        rc = blib.qlb_run_job(ctx._h, kv._h, layers, B, prefill, steps_, st.ctypes.data, hq_r,
+                              hkv_r, hd, w["theta"], code[w["in_dtype"]], code[w["out_dtype"]],
+                              *ptrs, comm._h if comm else None, hq, layer0)
         if rc != 0:
             raise qb.QllamaError(rc, qb.load().ql_last_error().decode())
+
+    def ptrs_all():
+        return [t.data_ptr() if t.numel() else None
+                for t in (pq, pk, pv, pout, dq, dk, dv, dout)]
 
     def rewind():
         """Back to the state before the step (pages kept), so it can be issued again."""
@@ -331,9 +433,9 @@ def run_ours(args, w):
 
     phases = []
     if P:
-        phases.append(("prefill", lambda: job(P, 0)))
+        phases.append(("prefill", lambda: run_job(0, Lyr, P, 0, lens0 + P, ptrs_all())))
     if D:
-        phases.append(("decode", lambda: job(0, D)))
+        phases.append(("decode", lambda: run_job(0, Lyr, 0, D, lens0 + P, ptrs_all())))
 
     # warm-up through the API (pages, workspace, RoPE table, kernel attributes),
     # then capture the same launches, one graph per phase
@@ -343,237 +445,302 @@ def run_ours(args, w):
     stream.synchronize()
     ctx.synchronize()
     rewind()
-    graphs = []
-    for name, fn in phases:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, stream=stream):
+    def capture(fn):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
             fn()
-        graphs.append((name, g))
+        return graph
+
+    graphs = [(pname, capture(fn)) for pname, fn in phases]
     rewind()
-    launches = {"job": Lyr * 2 + D * Lyr, "prefill": Lyr * 3, "decode": D * Lyr}[kind]
+    counted = [graph_kernel_nodes(g) for _, g in graphs]
+    if all(c is not None for c in counted):
+        launches, launch_src = sum(counted), "kernel nodes of the captured graphs"
+    else:
+        per_prefill = 3 if (hd in (64, 128) and w["kv"] in ("f16", "bf16") and P >= 64) else 2
+        launches = Lyr * per_prefill * (P > 0) + D * Lyr
+        if shard and P:
+            launches += Lyr  # the peer copy kernel of each prefill call
+        launch_src = "computed from the dispatch rules"
 
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
-
-    def barrier():
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         with torch.cuda.stream(stream):
             for _, g in graphs:
                 g.replay()
     stream.synchronize()
     ctx.synchronize()
     nph = len(graphs)
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(nph + 1)] for _ in range(args.steps)]
-    gpu_index = local
-    cvd = os.environ.get("CUDA_VISIBLE_DEVICES")
-    if cvd:
-        gpu_index = int(cvd.split(",")[local])
-    sampler = ClockSampler(gpu_index)
-    barrier()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(nph + 1)] for _ in range(steps)]
+    sampler = ClockSampler(env.gpu_index)
+    env.barrier()
     sampler.start()
     time.sleep(0.3)
-    for i in range(args.steps):
+    for i in range(steps):
         with torch.cuda.stream(stream):
-            flush.zero_()  # evict the previous step's data from L2 (outside the events)
+            env.flush.zero_()  # evict the previous step's data from L2 (outside the events)
             ev[i][0].record(stream)
             for p, (_, g) in enumerate(graphs):
                 g.replay()
                 ev[i][p + 1].record(stream)
-    barrier()
+    env.barrier()
     clocks = sampler.stop()
     ctx.synchronize()
     t_ph = [sum(e[p].elapsed_time(e[p + 1]) for e in ev) / 1e3 for p in range(nph)]
-    if world > 1:
-        tt = torch.tensor(t_ph, device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_ph = tt.tolist()
+    t_ph = env.max_over_ranks(t_ph)
     t_tot = sum(t_ph)
     ph = dict(zip([n for n, _ in graphs], t_ph))
+    del graphs  # released before the communicator (a graph may hold its NCCL calls)
 
-    # ---- algorithmic work of one step
+    # ---- algorithmic work of one step (this rank's share)
     hbm, bf16, which = peaks()
     eb, ib, ob = KV_BYTES[w["kv"]], IO_BYTES[w["in_dtype"]], IO_BYTES[w["out_dtype"]]
-    dec_bytes = 0.0
-    for s in range(D):
-        dec_bytes += Lyr * float(np.sum(lens0 + P + s + 1)) * hkv_r * hd * 2 * eb
-    dec_bytes += D * Lyr * B * ((hq_r + 4 * hkv_r) * hd * ib + hq * hd * ob)
+
+    def decode_bytes(start_lens):
+        tot = 0.0
+        for s in range(D):
+            tot += Lyr * float(np.sum(start_lens + s + 1)) * hkv_r * hd * 2 * eb
+        return tot + D * Lyr * B * ((hq_r + 4 * hkv_r) * hd * ib + hq * hd * ob)
+
+    dec_bytes = decode_bytes(lens0 + P)
     pre_flops = 4.0 * B * hq_r * hd * P * (P + 1) / 2 * Lyr
     tokens = B * (P + D)
     # bytes and FLOPs add up over the ranks; with sharded heads the tokens do not
     tok_mult = 1 if shard else world
-    step_value = {"job": tokens, "prefill": pre_flops / 1e12, "decode": dec_bytes / 1e9}[kind]
-    value = (tok_mult if kind == "job" else world) * args.steps * step_value / t_tot
+    step_value = {"job": tokens * tok_mult, "prefill": world * pre_flops / 1e12,
+                  "decode": world * dec_bytes / 1e9}[kind]
+    value = steps * step_value / t_tot
 
     # ---- e2e through the C ABI from pinned host memory
-    # The step's inputs come from pinned host memory and its outputs go back
-    # to it, every step, inside the timed region.  The copies run on a copy
-    # stream in chunks (the prefill inputs a few layers at a time, then the
-    # decode inputs a few token steps at a time) so that they overlap the
-    # calls, which wait for their chunk's inputs; each chunk's outputs are
-    # copied back once its calls end.
-    host_in = [t.cpu().pin_memory() for t in (pq, pk, pv, dq, dk, dv)]
-    host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (pout, dout)]
-    h2d = sum(t.numel() * t.element_size() for t in host_in)
-    d2h = sum(t.numel() * t.element_size() for t in host_out)
-    e2e_reps = max(1, min(args.steps, 3))
-    cstream = torch.cuda.Stream(device=dev)
-    chunk = max(1, (D + 7) // 8)  # decode steps per copy chunk
-    dchunks = [(c0, min(D, c0 + chunk)) for c0 in range(0, D, chunk)]
-    lchunk = max(1, (Lyr + 7) // 8)  # prefill layers per copy chunk
-    pchunks = [(c0, min(Lyr, c0 + lchunk)) for c0 in range(0, Lyr, lchunk)] if P else []
+    e2e = None
+    if with_e2e:
+        host_in = [t.cpu().pin_memory() for t in (pq, pk, pv, dq, dk, dv)]
+        host_out = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in (pout, dout)]
+        h2d = sum(t.numel() * t.element_size() for t in host_in)
+        d2h = sum(t.numel() * t.element_size() for t in host_out)
+        cstream = torch.cuda.Stream(device=dev)
+        chunk = max(1, (D + 7) // 8)  # decode steps per copy chunk
+        dchunks = [(c0, min(D, c0 + chunk)) for c0 in range(0, D, chunk)]
+        lchunk = max(1, (Lyr + 7) // 8)  # prefill layers per copy chunk
+        pchunks = [(c0, min(Lyr, c0 + lchunk)) for c0 in range(0, Lyr, lchunk)] if P else []
+        # decode workloads: each e2e step continues where the last one ended
+        e2e_start = [lens0 + P + (D * it if kind == "decode" else 0) for it in range(1 + e2e_reps)]
 
-    def job_steps(s0, s1):
-        """Decode steps [s0, s1) through the C ABI (inputs and outputs of those steps)."""
-        st = np.ascontiguousarray(lens0 + P + s0, dtype=np.int64)
-        ptrs = [None] * 4 + [t[s0].data_ptr() for t in (dq, dk, dv, dout)]
-        rc = blib.qlb_run_job(ctx._h, kv._h, Lyr, B, 0, s1 - s0, st.ctypes.data, hq_r, hkv_r, hd,
-                              w["theta"], code[w["in_dtype"]], code[w["out_dtype"]], *ptrs,
-                              comm._h if comm else None, hq, 0)
-        if rc != 0:
-            raise qb.QllamaError(rc, qb.load().ql_last_error().decode())
+        def e2e_step(it):
+            """Chunked copies in on `cstream`, the calls on `stream`, copies out."""
+            ev_c = torch.cuda.Event()
+            ev_c.record(stream)
+            cstream.wait_event(ev_c)  # the previous step's calls are done with the buffers
+            ready = []
+            with torch.cuda.stream(cstream):
+                for l0, l1 in pchunks:
+                    for dst, src in zip((pq, pk, pv), host_in[:3]):
+                        dst[l0:l1].copy_(src[l0:l1], non_blocking=True)
+                    e = torch.cuda.Event()
+                    e.record(cstream)
+                    ready.append(e)
+                for s0, s1 in dchunks:
+                    for dst, src in zip((dq, dk, dv), host_in[3:]):
+                        dst[s0:s1].copy_(src[s0:s1], non_blocking=True)
+                    e = torch.cuda.Event()
+                    e.record(cstream)
+                    ready.append(e)
+            with torch.cuda.stream(stream):
+                if kind != "decode":  # a new job: its pages go back to the pool
+                    for b in range(B):
+                        kv.clear_seq(b)
+                k = 0
+                for l0, l1 in pchunks:
+                    stream.wait_event(ready[k])
+                    k += 1
+                    run_job(l0, l1 - l0, P, 0, lens0 + P,
+                            [t[l0].data_ptr() for t in (pq, pk, pv, pout)] + [None] * 4)
+                    e = torch.cuda.Event()
+                    e.record(stream)
+                    cstream.wait_event(e)
+                    with torch.cuda.stream(cstream):
+                        host_out[0][l0:l1].copy_(pout[l0:l1], non_blocking=True)
+                for s0, s1 in dchunks:
+                    stream.wait_event(ready[k])
+                    k += 1
+                    run_job(0, Lyr, 0, s1 - s0, e2e_start[it] + s0,
+                            [None] * 4 + [t[s0].data_ptr() for t in (dq, dk, dv, dout)])
+                    e = torch.cuda.Event()
+                    e.record(stream)
+                    cstream.wait_event(e)
+                    with torch.cuda.stream(cstream):
+                        host_out[1][s0:s1].copy_(dout[s0:s1], non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(cstream)
+            stream.wait_event(done)  # the step ends when its outputs are in host memory
 
-    def job_layers(l0, l1):
-        """The prefill of cache layers [l0, l1) through the C ABI."""
-        st = np.ascontiguousarray(lens0 + P, dtype=np.int64)
-        ptrs = [t[l0].data_ptr() for t in (pq, pk, pv, pout)] + [None] * 4
-        rc = blib.qlb_run_job(ctx._h, kv._h, l1 - l0, B, P, 0, st.ctypes.data, hq_r, hkv_r, hd,
-                              w["theta"], code[w["in_dtype"]], code[w["out_dtype"]], *ptrs,
-                              comm._h if comm else None, hq, l0)
-        if rc != 0:
-            raise qb.QllamaError(rc, qb.load().ql_last_error().decode())
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        for it in range(1 + e2e_reps):
+            if it == 1:
+                env.barrier()
+                t0.record(stream)
+            e2e_step(it)
+        t1.record(stream)
+        env.barrier()
+        ctx.synchronize()
+        t_e2e = env.max_over_ranks([t0.elapsed_time(t1) / 1e3])[0]
+        if kind == "decode":
+            e2e_work = world * sum(decode_bytes(e2e_start[it]) for it in range(1, 1 + e2e_reps)) / 1e9
+        else:
+            e2e_work = e2e_reps * step_value
+        e2e = {"value": e2e_work / t_e2e, "unit": w["unit"], "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h,
+               "path": "qlb_run_job -> ql_attn_forward" + ("_sharded" if shard else "") +
+                       " per layer per token step (C ABI)",
+               "pages": ("decode steps continue past the timed step: sequences enter new pages"
+                         if kind == "decode" else
+                         "every step releases its pages (ql_kv_clear_seq) and reserves them again")}
 
-    def e2e_step():
-        """One step: chunked copies in on `cstream`, the calls on `stream`, copies out."""
-        ev_c = torch.cuda.Event()
-        ev_c.record(stream)
-        cstream.wait_event(ev_c)  # the previous step's calls are done with the buffers
-        ready = []
-        with torch.cuda.stream(cstream):
-            for l0, l1 in pchunks:
-                for dst, src in zip((pq, pk, pv), host_in[:3]):
-                    dst[l0:l1].copy_(src[l0:l1], non_blocking=True)
-                e = torch.cuda.Event()
-                e.record(cstream)
-                ready.append(e)
-            for s0, s1 in dchunks:
-                for dst, src in zip((dq, dk, dv), host_in[3:]):
-                    dst[s0:s1].copy_(src[s0:s1], non_blocking=True)
-                e = torch.cuda.Event()
-                e.record(cstream)
-                ready.append(e)
-        with torch.cuda.stream(stream):
-            rewind()
-            k = 0
-            for l0, l1 in pchunks:
-                stream.wait_event(ready[k])
-                k += 1
-                job_layers(l0, l1)
-                e = torch.cuda.Event()
-                e.record(stream)
-                cstream.wait_event(e)
-                with torch.cuda.stream(cstream):
-                    host_out[0][l0:l1].copy_(pout[l0:l1], non_blocking=True)
-            for s0, s1 in dchunks:
-                stream.wait_event(ready[k])
-                k += 1
-                job_steps(s0, s1)
-                e = torch.cuda.Event()
-                e.record(stream)
-                cstream.wait_event(e)
-                with torch.cuda.stream(cstream):
-                    host_out[1][s0:s1].copy_(dout[s0:s1], non_blocking=True)
-        done = torch.cuda.Event()
-        done.record(cstream)
-        stream.wait_event(done)  # the step ends when its outputs are in host memory
-
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    for it in range(1 + e2e_reps):
-        if it == 1:
-            barrier()
-            t0.record(stream)
-        e2e_step()
-    t1.record(stream)
-    barrier()
-    ctx.synchronize()
-    t_e2e = t0.elapsed_time(t1) / 1e3
-    if world > 1:
-        tt = torch.tensor([t_e2e], device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        t_e2e = tt.item()
-    e2e_value = (tok_mult if kind == "job" else world) * e2e_reps * step_value / t_e2e
-
-    # ---- roofline of the dominant kernel
+    # ---- roofline of the dominant kernel (per GPU)
     if kind == "prefill":
-        t_pre = ph["prefill"] / args.steps
+        t_pre = ph["prefill"] / steps
         achieved = pre_flops / t_pre / 1e12
-        roof = {"kernel": "prefill_tc_kernel<128> (tcgen05/TMEM causal attention)",
+        roof = {"kernel": f"prefill_tc_kernel<{hd}> (tcgen05/TMEM causal attention)",
                 "bound": "tensor", "achieved": achieved, "peak": bf16, "unit": "TFLOP/s",
                 "frac": achieved / bf16, "peak_source": which,
-                "traffic": ncu_traffic(args.workload, B, None),
+                "traffic": ncu_traffic(name, B, None) if not shard else None,
                 "flops_per_launch": pre_flops / Lyr, "launch_us": 1e6 * t_pre / Lyr,
                 "timed": "the whole call: append, rotated-q and attention kernels"}
     else:
-        t_dec = ph["decode"] / args.steps
+        t_dec = ph["decode"] / steps
         achieved = dec_bytes / t_dec / 1e9
         roof = {"kernel": f"splitkv_kernel<{hd},{w['kv']}> (fused RoPE+append+decode attention)",
                 "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                 "frac": achieved / hbm, "peak_source": which,
-                "traffic": ncu_traffic(args.workload, B, dec_bytes / (D * Lyr)),
+                "traffic": ncu_traffic(name, B, dec_bytes / (D * Lyr)) if not shard else None,
                 "bytes_per_launch": dec_bytes / (D * Lyr), "launch_us": 1e6 * t_dec / (D * Lyr),
                 "timed": "decode phase / launches, graph gaps included"}
+    phases_out = {}
+    if P:
+        tf = pre_flops / (ph["prefill"] / steps) / 1e12  # per GPU
+        phases_out["prefill"] = {"ms_per_step": 1e3 * ph["prefill"] / steps,
+                                 "tflops_per_gpu": tf, "frac_bf16_peak": tf / bf16}
+    if D:
+        gbs = dec_bytes / (ph["decode"] / steps) / 1e9  # per GPU
+        phases_out["decode"] = {"ms_per_step": 1e3 * ph["decode"] / steps,
+                                "kv_gbs_per_gpu": gbs, "frac_hbm": gbs / hbm,
+                                "tok_s": tok_mult * steps * B * D / ph["decode"]}
+    res = {"value": value, "unit": w["unit"], "steps": steps, "warmup": warmup,
+           "ms_per_step": 1e3 * t_tot / steps, "scaling": "strong" if shard else "weak",
+           "config": config_of(name, w, world), "roofline": roof, "phases": phases_out,
+           "e2e": e2e, "gpu_launches": launches * steps, "gpu_launches_source": launch_src,
+           "clocks": clocks}
+    if shard:
+        res["exchange"] = {"p2p": "attention kernel stores its rows into every rank's buffer "
+                                  "over NVLink (CUDA IPC mappings), bounded flag waits",
+                           "nccl": "local attention, ncclAllGather, head-major permute"}[comm_mode]
+    if comm:
+        comm.close()
+    kv.close()
+    del pq, pk, pv, dq, dk, dv, pout, dout
+    torch.cuda.empty_cache()
+    return res
+
+
+def check_sharded(env, mode):
+    """Max-abs difference between a head-sharded call's gathered output and one
+    GPU's call over all heads (rank 0), on the same seeded inputs: a decode step
+    (fused exchange) and a 64-token chunk (exchange after the attention)."""
+    torch, qb = env.torch, env.qb
+    world, rank = env.world, env.rank
+    hq, hkv, hd, theta, B, L = 64, 8, 128, 500000.0, 4, 1000
+    rng = np.random.default_rng(99)  # the same on every rank
+    kfull = rng.standard_normal((B, L, hkv, hd)).astype(np.float32)
+    vfull = rng.standard_normal((B, L, hkv, hd)).astype(np.float32)
+    qr, kr = qb.shard_heads(hq, hkv, world, rank)
+    mine = qb.KvCache(env.ctx, 1, L + 80, len(kr), hd, "f16", 64, B)
+    full = qb.KvCache(env.ctx, 1, L + 80, hkv, hd, "f16", 64, B) if rank == 0 else None
+    for b in range(B):  # the same cached rows in both (update() stores K as given)
+        mine.update(0, np.ascontiguousarray(kfull[b][:, kr.start:kr.stop]),
+                    np.ascontiguousarray(vfull[b][:, kr.start:kr.stop]), np.arange(L), seq=b)
+        if full:
+            full.update(0, kfull[b], vfull[b], np.arange(L), seq=b)
+    comm = env.comm(B * 64 * hq * hd * 4, mode)
+    worst = 0.0
+    start = L
+    for n in (1, 64):
+        q = rng.standard_normal((B, n, hq, hd)).astype(np.float32)
+        k = rng.standard_normal((B, n, hkv, hd)).astype(np.float32)
+        v = rng.standard_normal((B, n, hkv, hd)).astype(np.float32)
+        dq = torch.from_numpy(np.ascontiguousarray(q[:, :, qr.start:qr.stop])).to(env.dev).half()
+        dk = torch.from_numpy(np.ascontiguousarray(k[:, :, kr.start:kr.stop])).to(env.dev).half()
+        dv = torch.from_numpy(np.ascontiguousarray(v[:, :, kr.start:kr.stop])).to(env.dev).half()
+        with torch.cuda.stream(env.stream):
+            out = qb.attention_forward_sharded(comm, mine, 0, dq, dk, dv, [start] * B, len(qr),
+                                               len(kr), hd, theta, out_dtype="f32")
+        env.ctx.synchronize()
+        if full:
+            fq, fk, fv = (torch.from_numpy(x).to(env.dev).half() for x in (q, k, v))
+            with torch.cuda.stream(env.stream):
+                ref = qb.attention_forward(full, 0, fq, fk, fv, [start] * B, hq, hkv, hd, theta,
+                                           out_dtype="f32")
+            env.ctx.synchronize()
+            worst = max(worst, float((out - ref).abs().max().item()))
+        start += n
+    env.barrier()
+    comm.close()
+    mine.close()
+    if full:
+        full.close()
+    return worst if rank == 0 else None
+
+
+def run_ours(args, w):
+    env = Env()
+    torch = env.torch
+    world, rank = env.world, env.rank
+    steps, warmup = args.steps, args.warmup
+    head = measure(env, args.workload, w, steps, warmup)
+    extra = {}
+    if not args.only:
+        sub_steps, sub_warm = min(steps, 5), 3
+        if world == 1:
+            for name in ("c2", "c3", "c4", "c5"):
+                if name == args.workload:
+                    continue
+                r = measure(env, name, dict(WORKLOADS[name]), sub_steps, sub_warm)
+                if rank == 0 and not args.no_cpu_baseline:
+                    cb = cpu_sample(WORKLOADS[name])
+                    r["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind",
+                                                            "sample")}
+                extra[name] = r
+        else:
+            w5 = dict(WORKLOADS["c5"])
+            if sharded(w5, world):
+                for mode in ("p2p", "nccl"):
+                    r = measure(env, "c5", w5, sub_steps, sub_warm, comm_mode=mode)
+                    r["check_max_abs_err_vs_1gpu"] = check_sharded(env, mode)
+                    extra[f"c5_{mode}"] = r
     if rank == 0:
-        phases_out = {}
-        if P:
-            tf = world * args.steps * pre_flops / ph["prefill"] / 1e12
-            phases_out["prefill"] = {"ms_per_step": 1e3 * ph["prefill"] / args.steps,
-                                     "tflops": tf, "frac_bf16_peak": tf / bf16}
-        if D:
-            gbs = world * args.steps * dec_bytes / ph["decode"] / 1e9
-            phases_out["decode"] = {"ms_per_step": 1e3 * ph["decode"] / args.steps,
-                                    "kv_gbs": gbs, "frac_hbm": gbs / hbm,
-                                    "tok_s": tok_mult * args.steps * B * D / ph["decode"]}
+        hbm, bf16, which = peaks()
         line = {
-            "metric": METRIC, "value": value, "unit": w["unit"], "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * t_tot / args.steps,
-            "higher_is_better": True, "scaling": "strong" if shard else "weak",
-            "vs_baseline": None,
+            "metric": METRIC, "value": head["value"], "unit": head["unit"], "n_gpus": world,
+            "steps": steps, "warmup": warmup, "ms_per_step": head["ms_per_step"],
+            "higher_is_better": True, "scaling": head["scaling"], "vs_baseline": None,
             "dtype": "q8_0/f16" if w["kv"] == "q8_0" else "f16", "data": "synthetic",
-            "config": {"workload": args.workload, "desc": w["desc"], "layers": Lyr,
-                       "num_heads": hq, "num_kv_heads": hkv, "head_dim": hd, "kv_dtype": w["kv"],
-                       "batch_per_gpu": B, "prefill": P, "decode_steps": D,
-                       "page_size": w["page"],
-                       "l2": "flushed between steps (256 MB write outside the timed events)",
-                       "parallelism": (f"KV heads split over {world} GPUs ({hkv_r} KV / {hq_r} "
-                                       f"query heads each), outputs all-gathered over NVLink "
-                                       f"inside the decode kernel" if shard else
-                                       f"{world} independent replica(s), one per GPU"),
-                       "timing": "CUDA events around CUDA-graph replays of the API's launches"},
-            "roofline": roof, "phases": phases_out,
-            "e2e": {"value": e2e_value, "unit": w["unit"], "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h,
-                    "path": "qlb_run_job -> ql_attn_forward" + ("_sharded" if shard else "") +
-                            " per layer per token step (C ABI)"},
-            "gpu_launches": launches * args.steps,
-            "clocks": clocks,
+            "config": head["config"],
+            "l2": "flushed between steps (256 MB write outside the timed events)",
+            "timing": "CUDA events around CUDA-graph replays of the API's launches, max over ranks",
+            "roofline": head["roofline"], "phases": head["phases"], "e2e": head["e2e"],
+            "gpu_launches": head["gpu_launches"],
+            "gpu_launches_source": head["gpu_launches_source"], "clocks": head["clocks"],
+            "peaks": {"hbm_gbs": hbm, "bf16_tflops": bf16, "source": which},
         }
+        if "exchange" in head:
+            line["exchange"] = head["exchange"]
+        if extra:
+            line["workloads"] = extra
         if world == 1 and not args.no_cpu_baseline:
             cb = cpu_sample(w)
             line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind",
                                                        "sample")}
         print(json.dumps(line), flush=True)
-    del graphs
-    if comm:
-        comm.close()
-    kv.close()
-    ctx.close()
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    env.close()
 
 
 def main():
@@ -583,20 +750,24 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="c2")
+    ap.add_argument("--only", action="store_true",
+                    help="measure the chosen workload alone (no 'workloads' entries)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the workload's batch (a smaller case of the same shapes, "
                          "e.g. for an ncu capture; the line then names the changed config)")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count")
-    ap.add_argument("--shard", choices=("auto", "heads", "replicas"), default="auto",
-                    help="with several GPUs: split the KV heads (auto: the 70B-shaped decode) "
-                         "or run independent replicas")
+    ap.add_argument("--shard", choices=("auto", "replicas"), default="auto",
+                    help="with several GPUs: the workload's own split (auto) or replicas")
     args = ap.parse_args()
+    args.warmup = max(3, args.warmup)  # at least three untimed steps
     w = dict(WORKLOADS[args.workload])
     for key in ("batch", "layers"):
         if getattr(args, key) is not None:
             w[key] = getattr(args, key)
             w["desc"] += f" [{key} overridden to {w[key]}]"
+    if args.shard == "replicas":
+        w["shard_upto"] = 0
     if args.impl == "reference":
         run_reference(args, w)
     else:

@@ -18,6 +18,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <memory>
 #include <string>
@@ -117,6 +118,11 @@ struct ql_kv {
   // was named by the current call when seen_mark[s] == seen_epoch.
   std::vector<uint32_t> seen_mark;
   uint32_t seen_epoch = 0;
+  // Block-table entries handed out by the current call (index into `table`):
+  // the roll-back log on pool exhaustion and the list the table patch kernel
+  // uploads.  Reserved to the table's size at creation, so a call never
+  // grows it.
+  std::vector<int32_t> patch_idx;
 };
 
 namespace {
@@ -141,7 +147,7 @@ int ensure_counters(ql_ctx* c, size_t n) {
   c->counters_n = 0;
   size_t want = n + n / 2 + 1024;
   QL_CUDA(cudaMalloc(&c->counters, want * sizeof(int32_t)), "allocate counters");
-  QL_CUDA(cudaMemset(c->counters, 0, want * sizeof(int32_t)), "zero counters");
+  QL_CUDA(cudaMemsetAsync(c->counters, 0, want * sizeof(int32_t), c->stream), "zero counters");
   c->counters_n = want;
   return QL_OK;
 }
@@ -215,46 +221,70 @@ int ensure_rope(ql_kv* kv, float theta) {
     QL_CUDA(cudaMalloc(&kv->d_rope, std::max<size_t>(1, tab.size()) * sizeof(double2)),
             "allocate rope table");
   }
-  QL_CUDA(cudaStreamSynchronize(kv->ctx->stream), "synchronize before rope table upload");
-  QL_CUDA(cudaMemcpy(kv->d_rope, tab.data(), tab.size() * sizeof(double2),
-                     cudaMemcpyHostToDevice),
+  // On the context's stream (the kernels that read the table run there), and
+  // waited for before the host vector goes away.
+  QL_CUDA(cudaMemcpyAsync(kv->d_rope, tab.data(), tab.size() * sizeof(double2),
+                          cudaMemcpyHostToDevice, kv->ctx->stream),
           "upload rope table");
+  QL_CUDA(cudaStreamSynchronize(kv->ctx->stream), "wait for the rope table upload");
   kv->rope_theta = theta;
   return QL_OK;
 }
 
+// Queues the upload of the block-table entries listed in idx[0..n) (their
+// values taken from the host mirror) as table patch launches on the
+// context's stream: stream-ordered, with no host synchronisation.
+int upload_table_entries(ql_kv* kv, const int32_t* idx, size_t n) {
+  ql::TablePatch p;
+  p.table = kv->d_table;
+  for (size_t i0 = 0; i0 < n; i0 += ql::kTablePatchMax) {
+    const size_t m = std::min<size_t>(ql::kTablePatchMax, n - i0);
+    p.n = static_cast<int32_t>(m);
+    for (size_t i = 0; i < m; ++i) {
+      p.idx[i] = idx[i0 + i];
+      p.val[i] = kv->table[static_cast<size_t>(idx[i0 + i])];
+    }
+    QL_CUDA(ql::launch_table_patch(p, kv->ctx->stream), "launch block-table patch");
+  }
+  return QL_OK;
+}
+
 // Gives every listed sequence the pages its new length needs; rolls back on
-// exhaustion so that the call stays transactional.
-int reserve_pages(ql_kv* kv, const int32_t* seqs, const int64_t* ends, int count) {
+// exhaustion so that the call stays transactional.  New entries reach the
+// device through a table patch launch queued on the context's stream (no
+// host synchronisation, no per-call allocation); *patched tells the caller
+// that a split-KV launch following it must not use programmatic dependent
+// launch (that kernel reads the table before its grid dependency wait).
+int reserve_pages(ql_kv* kv, const int32_t* seqs, const int64_t* ends, int count, bool* patched) {
   const int P = kv->cfg.page_size, pps = kv->pages_per_seq;
-  std::vector<std::pair<int, int>> taken;  // (seq, logical page); grows only with new pages
-  bool changed = false;
+  *patched = false;
+  kv->patch_idx.clear();  // capacity reserved at creation: no allocation
   for (int i = 0; i < count; ++i) {
     const int s = seqs[i];
     const int need = static_cast<int>((ends[i] + P - 1) / P);
     while (kv->seq_pages[s] < need) {
       if (kv->free_pages.empty()) {
-        for (auto it = taken.rbegin(); it != taken.rend(); ++it) {
-          kv->free_pages.push_back(kv->table[static_cast<size_t>(it->first) * pps + it->second]);
-          kv->table[static_cast<size_t>(it->first) * pps + it->second] = -1;
-          kv->seq_pages[it->first]--;
+        for (auto it = kv->patch_idx.rbegin(); it != kv->patch_idx.rend(); ++it) {
+          kv->free_pages.push_back(kv->table[static_cast<size_t>(*it)]);
+          kv->table[static_cast<size_t>(*it)] = -1;
+          kv->seq_pages[*it / pps]--;
         }
+        kv->patch_idx.clear();
         return fail(QL_ERR_OOM, "KV page pool exhausted (%d pages of %d positions)",
                     kv->cfg.num_pages, P);
       }
       const int page = kv->free_pages.back();
       kv->free_pages.pop_back();
-      kv->table[static_cast<size_t>(s) * pps + kv->seq_pages[s]] = page;
-      taken.emplace_back(s, kv->seq_pages[s]);
+      const int32_t idx = s * pps + kv->seq_pages[s];
+      kv->table[static_cast<size_t>(idx)] = page;
+      kv->patch_idx.push_back(idx);
       kv->seq_pages[s]++;
-      changed = true;
     }
   }
-  if (changed) {
-    QL_CUDA(cudaStreamSynchronize(kv->ctx->stream), "synchronize before block-table upload");
-    QL_CUDA(cudaMemcpy(kv->d_table, kv->table.data(), kv->table.size() * sizeof(int32_t),
-                       cudaMemcpyHostToDevice),
-            "upload block table");
+  if (!kv->patch_idx.empty()) {
+    const int r = upload_table_entries(kv, kv->patch_idx.data(), kv->patch_idx.size());
+    if (r != QL_OK) return r;
+    *patched = true;
   }
   return QL_OK;
 }
@@ -277,7 +307,7 @@ int check_status(ql_ctx* c) {
   uint32_t st = 0;
   QL_CUDA(cudaMemcpy(&st, c->status, sizeof st, cudaMemcpyDeviceToHost), "read status word");
   if (st) {
-    cudaMemset(c->status, 0, sizeof(uint32_t));
+    cudaMemsetAsync(c->status, 0, sizeof(uint32_t), c->stream);
     return fail(QL_ERR_DEVICE, "a kernel reported status 0x%x (%s)", st,
                 (st & ql::kStatusPeerTimeout)   ? "another GPU of a head-sharded call did not "
                                                   "signal within the wait limit"
@@ -381,20 +411,25 @@ constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
-char* g_noalloc_addr[kMaxDevices] = {};  // device address of the array, per device
+// Device address of the array, per device (null until looked up).  Atomic,
+// because two host threads may make their first call on one device at once;
+// both then store the same address.
+std::atomic<char*> g_noalloc_addr[kMaxDevices] = {};
 
 // Called with `device` current.  The lookup runs once per device.
 int noalloc_scratch(int device, char** out) {
   if (device < 0 || device >= kMaxDevices)
     return fail(QL_ERR_UNSUPPORTED, "device %d is beyond the %d devices the scratch table covers",
                 device, kMaxDevices);
-  if (!g_noalloc_addr[device]) {
+  char* addr = g_noalloc_addr[device].load(std::memory_order_acquire);
+  if (!addr) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "look up the no-allocation scratch");
-    g_noalloc_addr[device] = static_cast<char*>(p);
+    addr = static_cast<char*>(p);
+    g_noalloc_addr[device].store(addr, std::memory_order_release);
   }
-  *out = g_noalloc_addr[device];
+  *out = addr;
   return QL_OK;
 }
 
@@ -427,7 +462,8 @@ int ql_ctx_create(int device, ql_ctx** out) {
   c->num_sms = prop.multiProcessorCount;
   e = cudaStreamCreateWithFlags(&c->own, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaMalloc(&c->status, sizeof(uint32_t));
-  if (e == cudaSuccess) e = cudaMemset(c->status, 0, sizeof(uint32_t));
+  if (e == cudaSuccess) e = cudaMemsetAsync(c->status, 0, sizeof(uint32_t), c->own);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->own);
   if (e != cudaSuccess) {
     ql_ctx_destroy(c);
     return cuda_fail(e, "create context");
@@ -514,14 +550,18 @@ int ql_kv_create(ql_ctx* c, const ql_kv_config* cfg_in, ql_kv** out) {
     }
   }
   kv->table.assign(static_cast<size_t>(cfg.max_batch) * std::max(1, kv->pages_per_seq), -1);
+  kv->patch_idx.reserve(kv->table.size());
   kv->seq_pages.assign(cfg.max_batch, 0);
   kv->seen_mark.assign(cfg.max_batch, 0);
+  kv->free_pages.reserve(cfg.num_pages);
   for (int p = cfg.num_pages - 1; p >= 0; --p) kv->free_pages.push_back(p);
   kv->len.assign(static_cast<size_t>(std::max(1, cfg.num_layers)) * cfg.max_batch, 0);
   cudaError_t e = cudaMalloc(&kv->d_table, kv->table.size() * sizeof(int32_t));
-  if (e == cudaSuccess)
-    e = cudaMemcpy(kv->d_table, kv->table.data(), kv->table.size() * sizeof(int32_t),
-                   cudaMemcpyHostToDevice);
+  // Every entry -1 (all bytes 0xff).  The pool memsets above ran on the legacy
+  // stream, which the context's non-blocking stream does not wait for: the
+  // device synchronisation orders all of them before any later launch.
+  if (e == cudaSuccess) e = cudaMemset(kv->d_table, 0xff, kv->table.size() * sizeof(int32_t));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return cleanup(cuda_fail(e, "allocate block table"));
   if (ql::splitkv_supported(cfg.head_dim, cfg.dtype, 1, cfg.page_size) && rows > 0) {
     kv->kmap.resize(cfg.num_layers);
@@ -569,11 +609,18 @@ int ql_kv_clear_seq(ql_kv* kv, int32_t seq) {
   if (kv->seq_pages[seq] > 0) {
     QL_CUDA(cudaSetDevice(kv->ctx->device), "set device");
     QL_CUDA(cudaStreamSynchronize(kv->ctx->stream), "synchronize before releasing pages");
+    kv->patch_idx.clear();
     for (int i = kv->seq_pages[seq] - 1; i >= 0; --i) {
-      kv->free_pages.push_back(kv->table[static_cast<size_t>(seq) * pps + i]);
-      kv->table[static_cast<size_t>(seq) * pps + i] = -1;
+      const int32_t idx = seq * pps + i;
+      kv->free_pages.push_back(kv->table[static_cast<size_t>(idx)]);
+      kv->table[static_cast<size_t>(idx)] = -1;
+      kv->patch_idx.push_back(idx);
     }
     kv->seq_pages[seq] = 0;
+    // the device table follows the mirror (-1: the slot owns no page)
+    const int r = upload_table_entries(kv, kv->patch_idx.data(), kv->patch_idx.size());
+    kv->patch_idx.clear();
+    if (r != QL_OK) return r;
   }
   return QL_OK;
 }
@@ -656,7 +703,8 @@ int ql_kv_update(ql_ctx* c, ql_kv* kv, int32_t layer, int32_t seq, const void* k
   QL_CUDA(cudaSetDevice(c->device), "set device");
   const int32_t one_seq = seq;
   const int64_t one_end = cur + n;
-  int r = reserve_pages(kv, &one_seq, &one_end, 1);
+  bool patched = false;  // append_kernel is an ordinary launch: it sees the patch
+  int r = reserve_pages(kv, &one_seq, &one_end, 1, &patched);
   if (r != QL_OK) return r;
   const size_t in_bytes = static_cast<size_t>(n) * hkv * hd * elem_bytes(in_dtype);
   const void *kd_ptr = k, *vd_ptr = v;
@@ -811,7 +859,8 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
     return fail(QL_ERR_UNSUPPORTED, "the fused head-sharded exchange needs a single-token "
                 "decode on the split-KV kernel");
   QL_CUDA(cudaSetDevice(c->device), "set device");
-  int r = reserve_pages(kv, seqs, ends, a->batch);
+  bool patched = false;
+  int r = reserve_pages(kv, seqs, ends, a->batch, &patched);
   if (r != QL_OK) return r;
   r = ensure_rope(kv, a->rope_theta);
   if (r != QL_OK) return r;
@@ -994,7 +1043,8 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
     at.out_vec = 1;  // symmetric buffers are 256-byte aligned
   }
   if (fast)
-    QL_CUDA(ql::launch_splitkv(at, &kv->kmap[layer], &kv->vmap[layer], jobs, c->stream),
+    QL_CUDA(ql::launch_splitkv(at, &kv->kmap[layer], &kv->vmap[layer], jobs, c->stream,
+                               /*pdl=*/!patched),
             "launch split-KV attention");
   else
     QL_CUDA(ql::launch_generic(at, c->stream), "launch attention");
@@ -1084,7 +1134,8 @@ int ql_attn_decode_noalloc(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   char* scratch = nullptr;
   int r = noalloc_scratch(c->device, &scratch);
   if (r != QL_OK) return r;
-  r = reserve_pages(kv, seqs, ends, a->batch);  // hands out pool pages; allocates nothing
+  bool patched = false;  // the launch below never uses programmatic dependent launch
+  r = reserve_pages(kv, seqs, ends, a->batch, &patched);  // hands out pool pages; allocates nothing
   if (r != QL_OK) return r;
   // Split plan of ql_attn_forward, with fewer splits if the partials would not fit.
   const int jobs = a->batch;
@@ -1290,7 +1341,8 @@ int ql_comm_create(ql_ctx* c, int nranks, int rank, const ql_comm_id* id,
     char* dh = nullptr;
     e = cudaMalloc(&dh, nranks * sizeof(Card));
     if (e == cudaSuccess)
-      e = cudaMemcpy(dh + rank * sizeof(Card), &mine, sizeof(Card), cudaMemcpyHostToDevice);
+      e = cudaMemcpyAsync(dh + rank * sizeof(Card), &mine, sizeof(Card), cudaMemcpyHostToDevice,
+                          c->stream);  // ordered before the all-gather on the same stream
     if (e != cudaSuccess) {
       if (dh) cudaFree(dh);
       return bail(cuda_fail(e, "stage the buffer cards"));

@@ -172,6 +172,17 @@ cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+// ----------------------------------------------------------- table patch --
+__global__ void __launch_bounds__(256) table_patch_kernel(const __grid_constant__ TablePatch p) {
+  for (int i = threadIdx.x; i < p.n; i += blockDim.x) p.table[p.idx[i]] = p.val[i];
+}
+
+cudaError_t launch_table_patch(const TablePatch& p, cudaStream_t s) {
+  if (p.n <= 0) return cudaSuccess;
+  table_patch_kernel<<<1, 256, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
 // --------------------------------------------------------------- generic --
 // One CTA per (query head, query token).  Bit-level restatement of the
 // reference's per-head loop (layers.rs:434-445) on the GPU.
@@ -618,9 +629,10 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   }
   __syncthreads();
   if (cl) cluster_arrive_relaxed();  // after the init fence: the others may now arrive on gbar
-  // Page ids of the first 32 tiles, one per producer lane.  Only the host
-  // writes the block table (synchronously, before any launch that reads it),
-  // so they are fetched before the stream dependency is met.
+  // Page ids of the first 32 tiles, one per producer lane, fetched before the
+  // stream dependency is met: the block table is written only by the table
+  // patch kernel, and a launch that follows a patch is an ordinary one (no
+  // programmatic dependency), so the entries are in place when this runs.
   const int* bt = a.cache.block_table + static_cast<size_t>(seq) * a.cache.pages_per_seq;
   int lane_page = 0;
   if (warp == NCW && lane < my_tiles) lane_page = __ldg(bt + (tile0 + lane) * kTile / a.cache.page);
@@ -628,7 +640,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   // now (prefetches read nothing into the CTA; lines written meanwhile are
   // updated in L2): the first stages' tiles, q of this KV head's group, the
   // rotation row and, for the appending CTA, the new K and V rows.
-  // The appending CTA's block-table entry for the new row, host-written too.
+  // The appending CTA's block-table entry for the new row (same rule).
   int app_page = -1;
   if (warp == NCW && appends)
     app_page = __ldg(bt + static_cast<size_t>(qpos) / a.cache.page);
@@ -1471,8 +1483,8 @@ int splitkv_ctas_per_sm(int hd, int dtype, bool device_rope) {
 }
 
 cudaError_t launch_splitkv(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,
-                           int jobs, cudaStream_t s) {
-  return dispatch_splitkv<false>(a, kmap, vmap, jobs, s, true);
+                           int jobs, cudaStream_t s, bool pdl) {
+  return dispatch_splitkv<false>(a, kmap, vmap, jobs, s, pdl);
 }
 
 cudaError_t launch_splitkv_device_rope(const AttnArgs& a, const CUtensorMap* kmap,

@@ -141,6 +141,17 @@ struct GatherArgs {
   CacheView cache;
 };
 
+// Block-table entries a call changed, carried in a kernel's parameter block
+// (copied at launch, so the host may reuse its arrays at once and nothing
+// waits for the copy).  table[idx[i]] = val[i].
+constexpr int kTablePatchMax = 1024;
+struct TablePatch {
+  int32_t* table;
+  int32_t n;
+  int32_t idx[kTablePatchMax];
+  int32_t val[kTablePatchMax];
+};
+
 // Dynamic shared memory the split-KV kernel needs for a configuration.
 size_t splitkv_smem_bytes(int hd, int dtype);
 // Whether the split-KV tensor-core kernel handles this configuration.
@@ -153,8 +164,11 @@ int splitkv_ctas_per_sm(int hd, int dtype, bool device_rope);
 int splitkv_wide_groups(int hd, int dtype);
 
 cudaError_t launch_append(const AppendArgs& a, cudaStream_t s);
+// pdl: launch with programmatic dependent launch (the kernel's set-up and its
+// block-table reads overlap the previous kernel).  Pass false when the
+// previous launch in the stream patched the block table.
 cudaError_t launch_splitkv(const AttnArgs& a, const CUtensorMap* kmap, const CUtensorMap* vmap,
-                           int grid_jobs, cudaStream_t s);
+                           int grid_jobs, cudaStream_t s, bool pdl = true);
 // Same kernel, with the RoPE angles computed on the device (f64 pow/sincos)
 // instead of read from the host-built table; needs fuse_append and new_len 1.
 cudaError_t launch_splitkv_device_rope(const AttnArgs& a, const CUtensorMap* kmap,
@@ -171,6 +185,12 @@ cudaError_t launch_peer_push(const void* src, int64_t rows, int row_bytes, int h
 cudaError_t launch_rank_to_head_major(const void* src, void* dst, int nranks, int64_t rows,
                                       int row_bytes, cudaStream_t s);
 cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s);
+// Writes the entries of `p` into the device block table, in stream order, as
+// an ordinary launch: a kernel queued after it sees the entries once its
+// stream dependency is met.  A split-KV launch that follows must not use
+// programmatic dependent launch, because that kernel reads the table before
+// its grid dependency wait.
+cudaError_t launch_table_patch(const TablePatch& p, cudaStream_t s);
 
 // tcgen05 prefill: when it applies, rows of the rotated-q scratch it needs,
 // and the launch (rotated-q kernel, then the attention kernel).

@@ -376,3 +376,48 @@ def test_truncate_rolls_back_and_rewrites(ctx):
     ref = oracle.attention_with_cache(fresh, 0, q[0], k[0], v[0], 60, hq, hkv, hd, theta)
     assert gu.max_err(out[0], ref) <= TOL_16
     assert p.gpu.layer_len(0, 0) == 61 and p.gpu.layer_len(1, 0) == 60
+
+
+def test_page_crossing_decode_never_waits_for_the_gpu(ctx):
+    """A ragged decode loop where some sequence enters a new page on every step.
+
+    The new block-table entries travel to the device in stream order (a table
+    patch launch), so the call returns while the GPU is still busy with work
+    queued before it: a long sleep kernel is queued first on the context's
+    stream, and the stream must still be busy when the call returns.  Every
+    step is checked against the oracle (cache.rs:83-170 semantics: the step
+    appends at current_len)."""
+    rng = np.random.default_rng(77)
+    hq, hkv, hd, theta, B = 16, 2, 64, 10000.0, 12
+    # step 0 warms up (RoPE table, workspace); sequence b enters a new
+    # 64-position page at step b + 1
+    starts = np.array([64 * (b % 3 + 1) - b - 1 for b in range(B)], np.int64)
+    p = gu.Pair(ctx, "f16", 2, 320, hkv, hd, B)
+    for s in range(B):
+        for layer in range(2):
+            p.prefill_rows(rng, layer, s, int(starts[s]), theta)
+    stream = torch.cuda.Stream()
+    ctx.set_stream(stream.cuda_stream)
+    try:
+        for step in range(B + 1):
+            crossing = [b for b in range(B) if (starts[b] % 64) == 0]
+            assert crossing == ([step - 1] if step else [])
+            for layer in range(2):
+                q, k, v = (gu.rounded(gu.normal(rng, (B, 1, h, hd)), "f16")
+                           for h in (hq, hkv, hkv))
+                dq, dk, dv = (gu.to_device(x, "f16") for x in (q, k, v))
+                out = torch.empty(B, 1, hq * hd, device="cuda", dtype=torch.float32)
+                torch.cuda.synchronize()
+                with torch.cuda.stream(stream):
+                    torch.cuda._sleep(200_000_000)  # ~0.1 s of GPU time queued first
+                qb.attention_forward(p.gpu, layer, dq, dk, dv, starts, hq, hkv, hd, theta,
+                                     out=out)
+                if step:
+                    assert not stream.query(), "the call waited for the GPU"
+                stream.synchronize()
+                ref = p.oracle_forward(layer, q, k, v, starts, hq, theta)
+                assert gu.max_err(out, ref) <= TOL_16, (step, layer)
+            starts = starts + 1
+        ctx.synchronize()
+    finally:
+        ctx.set_stream(None)
