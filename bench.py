@@ -446,7 +446,7 @@ def measure(env, name, w, steps, warmup, comm_mode="p2p", with_e2e=True):
     ctx.synchronize()
     rewind()
     def capture(fn):
-        graph = torch.cuda.CUDAGraph()
+        graph = torch.cuda.CUDAGraph(keep_graph=True)  # kept, so its nodes can be counted
         with torch.cuda.graph(graph, stream=stream):
             fn()
         return graph
@@ -454,10 +454,12 @@ def measure(env, name, w, steps, warmup, comm_mode="p2p", with_e2e=True):
     graphs = [(pname, capture(fn)) for pname, fn in phases]
     rewind()
     counted = [graph_kernel_nodes(g) for _, g in graphs]
+    for _, g in graphs:
+        g.instantiate()
     if all(c is not None for c in counted):
         launches, launch_src = sum(counted), "kernel nodes of the captured graphs"
     else:
-        per_prefill = 3 if (hd in (64, 128) and w["kv"] in ("f16", "bf16") and P >= 64) else 2
+        per_prefill = 2  # tcgen05 prefill: prologue + attention; else append + split-KV
         launches = Lyr * per_prefill * (P > 0) + D * Lyr
         if shard and P:
             launches += Lyr  # the peer copy kernel of each prefill call

@@ -10,6 +10,8 @@ which restates the reference's CPU arithmetic:
 * ``KvCache``         -- src/kv_cache/cache.rs:47-247
 * ``attention_with_cache`` -- src/transformer/layers.rs:397-455
 * ``attention_full``  -- src/transformer/layers.rs:293-351
+* ``silu``            -- src/tensor/ops.rs:222-239 (end-to-end model parity)
+* ``sample``          -- src/sampler/sampler.rs:119-325 (with the uniform draw given)
 
 Only the tests, ``__graft_entry__.smoke`` and the CPU-baseline leg of
 ``bench.py`` may import this package.  The product library never does.
@@ -88,6 +90,9 @@ def lib() -> ctypes.CDLL:
         L.qlo_get_threads.restype = ctypes.c_int
         L.qlo_batch_attention_core.argtypes = [f32p, ctypes.POINTER(f32p), ctypes.POINTER(f32p),
                                                _c_size_p, sz, sz, sz, sz, sz, f32p, ctypes.c_int]
+        L.qlo_silu.argtypes = [f32p, sz, f32p]
+        L.qlo_sample.argtypes = [f32p, sz, i32p, sz, ctypes.c_float, sz, ctypes.c_float,
+                                 ctypes.c_float, ctypes.c_double, i32p, cp, sz]
         _lib = L
     return _lib
 
@@ -286,3 +291,26 @@ def batch_attention_core(q_roped, k_caches, v_caches, num_heads, num_kv_heads, h
     if rc:
         raise OracleError("batched attention core failed")
     return out
+
+
+# ---- model-host pieces (end-to-end parity) --------------------------------
+
+def silu(x) -> np.ndarray:
+    """ops.rs:222-239 with libm expf, as Rust's f32::exp calls it."""
+    x = _f32(x)
+    out = np.empty_like(x)
+    lib().qlo_silu(_fp(x), x.size, _fp(out))
+    return out
+
+
+def sample(logits, context, temperature: float, top_k: int, top_p: float,
+           repeat_penalty: float, r: float) -> int:
+    """Sampler::sample_slice (sampler.rs:119-325) with the uniform draw r in [0, 1)."""
+    lg = _f32(logits).ravel()
+    ctx = np.ascontiguousarray(np.asarray(context, dtype=np.int32).ravel())
+    out = ctypes.c_int32()
+    e = _err()
+    _check(lib().qlo_sample(_fp(lg), lg.size, ctx.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
+                            ctx.size, temperature, top_k, top_p, repeat_penalty, r,
+                            ctypes.byref(out), e, 512), e)
+    return out.value

@@ -572,3 +572,162 @@ int qlo_batch_attention_core(const float* qr, const float* const* kc, const floa
   (void)threads;
   return failed;
 }
+
+/* ---- model-host pieces outside attention --------------------------------- */
+
+/* ops.rs:222-239 */
+void qlo_silu(const float* x, size_t n, float* out) {
+  for (size_t i = 0; i < n; ++i) {
+    const float v = x[i];
+    if (v == -INFINITY) {
+      out[i] = -0.0f;
+    } else if (v >= 0.0f) {
+      const float d = 1.0f + expf(-v);
+      out[i] = v / d;
+    } else {
+      const float e = expf(v);
+      const float num = v * e;
+      const float d = 1.0f + e;
+      out[i] = num / d;
+    }
+  }
+}
+
+/* f32::total_cmp as an integer key: negative values reversed below positive. */
+static int32_t total_key(float f) {
+  int32_t b;
+  memcpy(&b, &f, 4);
+  return b ^ (int32_t)(((uint32_t)(b >> 31)) >> 1);
+}
+
+/* sorted_indices (sampler.rs:296-304): probability descending, id ascending. */
+static const double* g_sort_p;
+static int cmp_prob_desc(const void* a, const void* b) {
+  const size_t ia = *(const size_t*)a, ib = *(const size_t*)b;
+  const double pa = g_sort_p[ia], pb = g_sort_p[ib];
+  if (pa > pb) return -1;
+  if (pa < pb) return 1;
+  return ia < ib ? -1 : (ia > ib ? 1 : 0);
+}
+
+static size_t* sorted_indices(const double* p, size_t n) {
+  size_t* order = (size_t*)malloc(n * sizeof(size_t));
+  for (size_t i = 0; i < n; ++i) order[i] = i;
+  g_sort_p = p;
+  qsort(order, n, sizeof(size_t), cmp_prob_desc);
+  return order;
+}
+
+/* apply_top_k / apply_top_p share this: keep order[0..keep), renormalise. */
+static void keep_prefix(double* p, size_t n, const size_t* order, size_t keep) {
+  double total = 0.0;
+  for (size_t i = 0; i < keep; ++i) total += p[order[i]];
+  unsigned char* flags = (unsigned char*)calloc(n, 1);
+  for (size_t i = 0; i < keep; ++i) flags[order[i]] = 1;
+  for (size_t i = 0; i < n; ++i) p[i] = flags[i] ? p[i] / total : 0.0;
+  free(flags);
+}
+
+int qlo_sample(const float* logits, size_t vocab, const int32_t* context, size_t n_context,
+               float temperature, size_t top_k, float top_p, float repeat_penalty, double r,
+               int32_t* out, char* err, size_t errlen) {
+  if (vocab == 0) return fail(err, errlen, "Sampling requires a non-empty logits slice");
+  for (size_t i = 0; i < vocab; ++i)
+    if (!isfinite(logits[i]))
+      return fail(err, errlen, "Logits must be finite, but element %zu is %g", i,
+                  (double)logits[i]);
+  if (!isfinite(temperature))
+    return fail(err, errlen, "Sampler temperature must be finite, got %g", (double)temperature);
+  if (!isfinite(top_p)) return fail(err, errlen, "Sampler top_p must be finite, got %g", (double)top_p);
+  if (!isfinite(repeat_penalty) || repeat_penalty <= 0.0f)
+    return fail(err, errlen, "Sampler repeat_penalty must be finite and positive, got %g",
+                (double)repeat_penalty);
+  float* w = (float*)malloc(vocab * sizeof(float));
+  memcpy(w, logits, vocab * sizeof(float));
+  if (repeat_penalty != 1.0f) { /* apply_repeat_penalty */
+    unsigned char* seen = (unsigned char*)calloc(vocab, 1);
+    for (size_t i = 0; i < n_context; ++i) {
+      const int32_t t = context[i];
+      if (t < 0 || (size_t)t >= vocab || seen[t]) continue;
+      seen[t] = 1;
+      if (w[t] <= 0.0f) w[t] = w[t] * repeat_penalty;
+      else w[t] = w[t] / repeat_penalty;
+    }
+    free(seen);
+    for (size_t i = 0; i < vocab; ++i)
+      if (!isfinite(w[i])) {
+        free(w);
+        return fail(err, errlen, "Repeat penalty produced a non-finite logit at element %zu", i);
+      }
+  }
+  if (temperature <= 0.0f) { /* argmax: total order, ties to the smaller id */
+    size_t best = 0;
+    for (size_t i = 1; i < vocab; ++i)
+      if (total_key(w[i]) > total_key(w[best])) best = i;
+    free(w);
+    *out = (int32_t)best;
+    return 0;
+  }
+  for (size_t i = 0; i < vocab; ++i) {
+    w[i] = w[i] / temperature;
+    if (!isfinite(w[i])) {
+      free(w);
+      return fail(err, errlen, "Temperature %g produced a non-finite logit at element %zu",
+                  (double)temperature, i);
+    }
+  }
+  /* softmax (sampler.rs:226-235) */
+  float mx = -INFINITY;
+  for (size_t i = 0; i < vocab; ++i) mx = fmaxf(mx, w[i]);
+  double* p = (double*)malloc(vocab * sizeof(double));
+  double total = 0.0;
+  for (size_t i = 0; i < vocab; ++i) p[i] = exp((double)w[i] - (double)mx);
+  for (size_t i = 0; i < vocab; ++i) total += p[i];
+  for (size_t i = 0; i < vocab; ++i) p[i] = p[i] / total;
+  free(w);
+  if (top_k != 0 && top_k < vocab) { /* apply_top_k */
+    size_t* order = sorted_indices(p, vocab);
+    keep_prefix(p, vocab, order, top_k);
+    free(order);
+  }
+  if (top_p < 1.0f) { /* apply_top_p */
+    size_t* order = sorted_indices(p, vocab);
+    const double th = (double)top_p;
+    double cum = 0.0;
+    size_t keep = vocab;
+    for (size_t i = 0; i < vocab; ++i) {
+      cum += p[order[i]];
+      if (cum >= th) {
+        keep = i + 1;
+        break;
+      }
+    }
+    keep_prefix(p, vocab, order, keep);
+    free(order);
+  }
+  /* sample_from_distribution (sampler.rs:306-325) */
+  double t = 0.0;
+  for (size_t i = 0; i < vocab; ++i) t += p[i];
+  const double threshold = r * t;
+  double cum = 0.0;
+  long found = -1, last = -1;
+  for (size_t i = 0; i < vocab; ++i) {
+    if (p[i] <= 0.0) continue;
+    cum += p[i];
+    if (cum >= threshold) {
+      found = (long)i;
+      break;
+    }
+  }
+  if (found < 0)
+    for (size_t i = vocab; i-- > 0;)
+      if (p[i] > 0.0) {
+        last = (long)i;
+        break;
+      }
+  free(p);
+  if (found < 0 && last < 0)
+    return fail(err, errlen, "Sampling failed: the distribution has no positive probability");
+  *out = (int32_t)(found >= 0 ? found : last);
+  return 0;
+}

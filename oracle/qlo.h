@@ -113,6 +113,23 @@ int qlo_batch_attention_core(const float* qr, const float* const* kc, const floa
                              size_t num_heads, size_t num_kv_heads, size_t head_dim,
                              float* out, int threads);
 
+/* ---- model-host pieces outside attention (end-to-end parity only) ---- */
+/* TensorOps::silu (ops.rs:222-239): -inf -> -0.0; x >= 0: x / (1 + expf(-x));
+ * else e = expf(x), x * e / (1 + e); f32 with libm expf, as Rust's f32::exp. */
+void qlo_silu(const float* x, size_t n, float* out);
+
+/* Sampler::sample_slice (src/sampler/sampler.rs:119-325) with the uniform
+ * draw `r` in [0, 1) given instead of drawn from the seeded generator:
+ * repeat penalty (each context id once, out-of-range ids ignored), greedy
+ * argmax (total order, ties to the smaller id) when temperature <= 0, else
+ * temperature, softmax (f32 max, f64 exp, sequential f64 sum), top-k, top-p
+ * (sorted by probability descending then id ascending, sums in that order)
+ * and the draw in index order.  Returns 0 and the id, or nonzero with the
+ * reference's message. */
+int qlo_sample(const float* logits, size_t vocab, const int32_t* context, size_t n_context,
+               float temperature, size_t top_k, float top_p, float repeat_penalty, double r,
+               int32_t* out, char* err, size_t errlen);
+
 #ifdef __cplusplus
 }
 #endif

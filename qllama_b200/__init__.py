@@ -38,6 +38,10 @@ EXPORTS = (
     "ql_kv_seq_len", "ql_kv_layer_len", "ql_kv_update", "ql_kv_get", "ql_attn_forward",
     "ql_attn_decode_noalloc", "ql_kv_truncate", "ql_comm_unique_id", "ql_comm_create",
     "ql_comm_destroy", "ql_comm_buffer", "ql_attn_forward_sharded",
+    # include/qllama_model.h
+    "ql_llama_create", "ql_llama_destroy", "ql_llama_get_config", "ql_llama_set_tensor",
+    "ql_llama_load_gguf", "ql_llama_forward", "ql_sample", "ql_llama_generate",
+    "ql_qkv_rope_append", "ql_attn_forward_appended",
 )
 
 COMM_P2P, COMM_NCCL = 0, 1
@@ -120,6 +124,9 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
     L.ql_comm_destroy.argtypes = [vp]
     L.ql_comm_buffer.argtypes = [vp, ctypes.POINTER(vp), ctypes.POINTER(ctypes.c_uint64)]
     L.ql_attn_forward_sharded.argtypes = [vp, vp, vp, ctypes.POINTER(AttnArgs)]
+    from . import model as _model
+
+    _model.bind(L)
     for name in EXPORTS:
         if name not in ("ql_version", "ql_last_error"):
             getattr(L, name).restype = ctypes.c_int

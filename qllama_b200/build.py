@@ -8,8 +8,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libqllama_attn.so")
 BENCH_LIB = os.path.join(HERE, "libqllama_bench.so")
-SOURCES = ["ql_api.cu", "ql_kernels.cu", "ql_prefill_tc.cu"]
-HEADERS = ["ql_device.cuh", "ql_kernels.cuh", os.path.join("..", "..", "include", "qllama_attn.h")]
+SOURCES = ["ql_api.cu", "ql_kernels.cu", "ql_prefill_tc.cu", "ql_model.cu", "ql_gguf.cpp"]
+HEADERS = ["ql_device.cuh", "ql_kernels.cuh", "ql_append.cuh", "ql_internal.h",
+           os.path.join("..", "..", "include", "qllama_model.h"), os.path.join("..", "..", "include", "qllama_attn.h")]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -26,6 +26,7 @@
 
 #include "../../include/qllama_attn.h"
 #include "ql_device.cuh"
+#include "ql_internal.h"
 #include "ql_kernels.cuh"
 
 namespace {
@@ -87,17 +88,16 @@ EncodeTiledFn encode_tiled() {
 }  // namespace
 
 // --------------------------------------------------------------- context --
-struct ql_ctx {
-  int device = 0;
-  int num_sms = 0;
-  cudaStream_t own = nullptr;
-  cudaStream_t stream = nullptr;
-  uint32_t* status = nullptr;  // device word raised by kernels
-  void* ws = nullptr;          // workspace (staging, split partials, scratch)
-  size_t ws_bytes = 0;
-  int32_t* counters = nullptr;  // split-merge arrival counters, kept at zero
-  size_t counters_n = 0;
-};
+// struct ql_ctx is defined in ql_internal.h (the model host uses it too).
+int ql_fail(int code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_error = buf;
+  return code;
+}
 
 struct ql_kv {
   ql_ctx* ctx = nullptr;
@@ -113,6 +113,7 @@ struct ql_kv {
   std::vector<int32_t> free_pages;     // stack of free page ids
   std::vector<int64_t> len;            // [layer][seq] written prefix
   double2* d_rope = nullptr;           // [max_seq_len][head_dim/2] (cos, sin)
+  double2* d_rope_id = nullptr;        // [head_dim/2] (1, 0): queries that arrive rotated
   float rope_theta = 0.f;
   // Duplicate-sequence check of a call without per-call allocation: slot s
   // was named by the current call when seen_mark[s] == seen_epoch.
@@ -220,6 +221,13 @@ int ensure_rope(ql_kv* kv, float theta) {
   if (!kv->d_rope) {
     QL_CUDA(cudaMalloc(&kv->d_rope, std::max<size_t>(1, tab.size()) * sizeof(double2)),
             "allocate rope table");
+    // the identity rotation (cos 1, sin 0 leaves a pair exactly as it is)
+    std::vector<double2> id(std::max(1, pairs), make_double2(1.0, 0.0));
+    QL_CUDA(cudaMalloc(&kv->d_rope_id, id.size() * sizeof(double2)), "allocate rope table");
+    QL_CUDA(cudaMemcpyAsync(kv->d_rope_id, id.data(), id.size() * sizeof(double2),
+                            cudaMemcpyHostToDevice, kv->ctx->stream),
+            "upload the identity rotation");
+    QL_CUDA(cudaStreamSynchronize(kv->ctx->stream), "wait for the identity rotation");
   }
   // On the context's stream (the kernels that read the table run there), and
   // waited for before the host vector goes away.
@@ -303,7 +311,16 @@ int64_t& len_at(ql_kv* kv, int layer, int seq) {
   return kv->len[static_cast<size_t>(layer) * kv->cfg.max_batch + seq];
 }
 
-int check_status(ql_ctx* c) {
+}  // namespace
+
+int ql_ctx_workspace(ql_ctx* c, size_t bytes, void** out) {
+  const int r = ensure_ws(c, bytes);
+  if (r != QL_OK) return r;
+  *out = c->ws;
+  return QL_OK;
+}
+
+int ql_check_status(ql_ctx* c) {
   uint32_t st = 0;
   QL_CUDA(cudaMemcpy(&st, c->status, sizeof st, cudaMemcpyDeviceToHost), "read status word");
   if (st) {
@@ -312,10 +329,14 @@ int check_status(ql_ctx* c) {
                 (st & ql::kStatusPeerTimeout)   ? "another GPU of a head-sharded call did not "
                                                   "signal within the wait limit"
                 : (st & ql::kStatusWaitTimeout) ? "a pipeline wait timed out"
+                : (st & ql::kStatusBadLogits)   ? "the sampler met a non-finite logit"
+                : (st & ql::kStatusBadToken)    ? "a token id was outside the vocabulary"
                                                 : "a block-table entry was out of range");
   }
   return QL_OK;
 }
+
+namespace {
 
 // Split plan of the split-KV decode kernel: the 64-position tiles each CTA
 // streams, and the most splits any (token, KV head) job is cut into.
@@ -495,7 +516,7 @@ int ql_ctx_synchronize(ql_ctx* c) {
   if (!c) return fail(QL_ERR_INVALID, "ql_ctx_synchronize: ctx is NULL");
   QL_CUDA(cudaSetDevice(c->device), "set device");
   QL_CUDA(cudaStreamSynchronize(c->stream), "synchronize");
-  return check_status(c);
+  return ql_check_status(c);
 }
 
 int ql_kv_create(ql_ctx* c, const ql_kv_config* cfg_in, ql_kv** out) {
@@ -587,6 +608,7 @@ int ql_kv_destroy(ql_kv* kv) {
   for (void* p : kv->vs) cudaFree(p);
   if (kv->d_table) cudaFree(kv->d_table);
   if (kv->d_rope) cudaFree(kv->d_rope);
+  if (kv->d_rope_id) cudaFree(kv->d_rope_id);
   delete kv;
   return QL_OK;
 }
@@ -782,8 +804,11 @@ int ql_kv_get(ql_ctx* c, const ql_kv* kv, int32_t layer, int32_t seq, const int3
 
 // The operator.  With `peer` (a head-sharded single-token decode), the
 // split-KV kernel stores its rows into every rank's output instead of a->out.
+// appended: the call's K/V rows are already in the cache (written by
+// ql_qkv_rope_append at positions start_pos .. start_pos+new_len-1) and q
+// arrives rotated, so nothing is appended and q is not rotated again.
 static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
-                             const ql::PeerOut* peer) {
+                             const ql::PeerOut* peer, bool appended = false) {
   if (!c || !kv || !a) return fail(QL_ERR_INVALID, "ql_attn_forward: NULL argument");
   const int hq = a->num_heads, hkv = a->num_kv_heads, hd = a->head_dim;
   // Attention::new (layers.rs:254-261)
@@ -834,7 +859,13 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
       return fail(QL_ERR_INVALID, "position %lld exceeds the i32 range the cache uses",
                   (long long)last);
     const int64_t cur = len_at(kv, layer, s);
-    if (n > 0) {
+    if (n > 0 && appended) {
+      if (start + n != cur)
+        return fail(QL_ERR_INVALID,
+                    "the rows of positions %lld..%lld are not the last ones appended "
+                    "(current_len %lld)", (long long)start, (long long)(start + n - 1),
+                    (long long)cur);
+    } else if (n > 0) {
       if (start != cur)
         return fail(QL_ERR_INVALID,
                     "positions[0] = %lld must continue from current_len (expected %lld); "
@@ -853,14 +884,17 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
     ends[b] = start + n;
   }
   if (n == 0) return QL_OK;  // empty batch (transformer_forward.rs:919-946)
-  if (!a->q || !a->k || !a->v || !a->out) return fail(QL_ERR_INVALID, "q/k/v/out is NULL");
+  if (!a->q || (!appended && (!a->k || !a->v)) || !a->out)
+    return fail(QL_ERR_INVALID, "q/k/v/out is NULL");
+  if (appended && peer)
+    return fail(QL_ERR_UNSUPPORTED, "a head-sharded call appends its own rows");
   if (peer && !(n == 1 && a->mem == QL_MEM_DEVICE && kv->have_maps &&
                 ql::splitkv_supported(hd, kv->cfg.dtype, hq / hkv, kv->cfg.page_size)))
     return fail(QL_ERR_UNSUPPORTED, "the fused head-sharded exchange needs a single-token "
                 "decode on the split-KV kernel");
   QL_CUDA(cudaSetDevice(c->device), "set device");
   bool patched = false;
-  int r = reserve_pages(kv, seqs, ends, a->batch, &patched);
+  int r = appended ? QL_OK : reserve_pages(kv, seqs, ends, a->batch, &patched);
   if (r != QL_OK) return r;
   r = ensure_rope(kv, a->rope_theta);
   if (r != QL_OK) return r;
@@ -952,8 +986,12 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
   void* out = a->out;
   if (a->mem == QL_MEM_HOST) {
     QL_CUDA(cudaMemcpyAsync(w + o_q, a->q, qn * ib, cudaMemcpyHostToDevice, c->stream), "copy q");
-    QL_CUDA(cudaMemcpyAsync(w + o_k, a->k, kn * ib, cudaMemcpyHostToDevice, c->stream), "copy k");
-    QL_CUDA(cudaMemcpyAsync(w + o_v, a->v, kn * ib, cudaMemcpyHostToDevice, c->stream), "copy v");
+    if (!appended) {
+      QL_CUDA(cudaMemcpyAsync(w + o_k, a->k, kn * ib, cudaMemcpyHostToDevice, c->stream),
+              "copy k");
+      QL_CUDA(cudaMemcpyAsync(w + o_v, a->v, kn * ib, cudaMemcpyHostToDevice, c->stream),
+              "copy v");
+    }
     q = w + o_q;
     k = w + o_k;
     v = w + o_v;
@@ -965,20 +1003,24 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
     st.seq[b] = seqs[b];
     st.start[b] = static_cast<int32_t>(a->start_pos[b]);
   }
-  const bool fuse = fast && n == 1;
-  if (!fuse) {
-    ql::AppendArgs ap{};
-    ap.k = k;
-    ap.v = v;
-    ap.in_dtype = a->in_dtype;
-    ap.batch = a->batch;
-    ap.new_len = n;
-    ap.rope = kv->d_rope;
-    ap.cache = cv;
-    ap.status = c->status;
-    ap.seqs = st;
+  const bool fuse = fast && n == 1 && !appended;
+  ql::AppendArgs ap{};
+  ap.k = k;
+  ap.v = v;
+  ap.in_dtype = a->in_dtype;
+  ap.batch = a->batch;
+  ap.new_len = appended ? 0 : n;  // no rows for the prefill prologue to append
+  ap.rope = kv->d_rope;
+  ap.cache = cv;
+  ap.status = c->status;
+  ap.seqs = st;
+  // the tcgen05 prefill appends in its prologue kernel; a single-token decode
+  // on the split-KV kernel appends inside that kernel
+  if (!fuse && !tc_prefill && !appended)
     QL_CUDA(ql::launch_append(ap, c->stream), "launch append");
-  }
+  // queries: rotated here with the position's row, or taken as they are
+  const double2* q_rope = appended ? kv->d_rope_id : kv->d_rope;
+  const int32_t q_rope_stride = appended ? 0 : hd / 2;
   if (tc_prefill) {
     ql::PrefillArgs pa{};
     pa.q = q;
@@ -987,19 +1029,21 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
     pa.q_rows = static_cast<int32_t>(q_rows);
     pa.out = out;
     pa.out_dtype = a->out_dtype;
-    pa.rope = kv->d_rope;
+    pa.rope = q_rope;
+    pa.rope_stride = q_rope_stride;
     pa.cache = cv;
     pa.hq = hq;
     pa.group = group;
     pa.batch = a->batch;
     pa.new_len = n;
     pa.scale = 1.0f / std::sqrt(static_cast<float>(hd));  // layers.rs:432
+    pa.num_sms = c->num_sms;
     pa.status = c->status;
     pa.seqs = st;
     CUtensorMap qmap;
     r = encode_q_map(&qmap, w + o_qr, hd, static_cast<uint64_t>(a->batch) * hq * q_rows);
     if (r != QL_OK) return r;
-    QL_CUDA(ql::launch_prefill_tc(pa, &qmap, &kv->kmap[layer], &kv->vmap[layer], c->stream),
+    QL_CUDA(ql::launch_prefill_tc(pa, ap, &qmap, &kv->kmap[layer], &kv->vmap[layer], c->stream),
             "launch tcgen05 prefill");
     if (a->mem == QL_MEM_HOST) {
       QL_CUDA(cudaMemcpyAsync(a->out, out, qn * obb, cudaMemcpyDeviceToHost, c->stream),
@@ -1016,7 +1060,8 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
   at.in_dtype = a->in_dtype;
   at.out = out;
   at.out_dtype = a->out_dtype;
-  at.rope = kv->d_rope;
+  at.rope = q_rope;
+  at.rope_stride = q_rope_stride;
   at.cache = cv;
   at.hq = hq;
   at.group = group;
@@ -1060,6 +1105,87 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
 int ql_attn_forward(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   return attn_forward_impl(c, kv, a, nullptr);
 }
+
+int ql_attn_forward_appended(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
+  return attn_forward_impl(c, kv, a, nullptr, true);
+}
+
+}  // extern "C"
+
+// Library-internal half of ql_qkv_rope_append (ql_model.cu): validates the
+// call's positions like KvCache::update (cache.rs:90-144), gives the
+// sequences the pages they need (a table patch launch, no host
+// synchronisation) and the RoPE table, and reports where the rows go.  The
+// caller launches the kernel that writes them, then ql_kv_append_commit.
+int ql_kv_append_prepare(ql_ctx* c, ql_kv* kv, const ql_attn_args* a, ql::CacheView* view,
+                         const double2** rope, ql::SeqTable* st) {
+  if (!c || !kv || !a) return fail(QL_ERR_INVALID, "ql_qkv_rope_append: NULL argument");
+  const int hq = a->num_heads, hkv = a->num_kv_heads, hd = a->head_dim;
+  if (hq <= 0 || hkv <= 0 || hd <= 0)
+    return fail(QL_ERR_INVALID, "Attention head counts and head_dim must be positive");
+  if (hq % hkv != 0)
+    return fail(QL_ERR_INVALID, "num_heads %d must be divisible by num_kv_heads %d", hq, hkv);
+  if ((hd & 1) != 0)
+    return fail(QL_ERR_INVALID,
+                "RoPE requires shape [seq_len, ..., head_dim] with a positive even head_dim");
+  if (!std::isfinite(a->rope_theta) || a->rope_theta <= 0.f)
+    return fail(QL_ERR_INVALID, "RoPE theta must be finite and positive");
+  if (a->batch < 1 || a->new_len < 0 || a->batch > ql::kMaxBatch || a->batch > kv->cfg.max_batch)
+    return fail(QL_ERR_INVALID, "batch %d / new_len %d outside the limits", a->batch, a->new_len);
+  if (!a->seq_ids || !a->start_pos) return fail(QL_ERR_INVALID, "seq_ids/start_pos are NULL");
+  const int layer = a->layer_idx;
+  if (layer < 0 || layer >= kv->cfg.num_layers)
+    return fail(QL_ERR_INVALID, "KV cache layer index %d out of range (cache has %d layers)",
+                layer, kv->cfg.num_layers);
+  if (hkv != kv->cfg.num_kv_heads || hd != kv->cfg.head_dim)
+    return fail(QL_ERR_INVALID, "K shape [%d, %d, %d] does not match cache [_, %d, %d]",
+                a->new_len, hkv, hd, kv->cfg.num_kv_heads, kv->cfg.head_dim);
+  if (kv->cfg.dtype == QL_Q8_0)
+    return fail(QL_ERR_UNSUPPORTED, "the fused projection appends f32, f16 or bf16 rows; a Q8_0 "
+                "cache takes ql_attn_forward");
+  const int n = a->new_len;
+  int32_t seqs[ql::kMaxBatch];
+  int64_t ends[ql::kMaxBatch];
+  const uint32_t mark = next_seen_epoch(kv);
+  for (int b = 0; b < a->batch; ++b) {
+    const int s = a->seq_ids[b];
+    if (s < 0 || s >= kv->cfg.max_batch)
+      return fail(QL_ERR_INVALID, "sequence %d out of range (cache has %d slots)", s,
+                  kv->cfg.max_batch);
+    if (kv->seen_mark[s] == mark)
+      return fail(QL_ERR_INVALID, "sequence %d appears twice in one call", s);
+    kv->seen_mark[s] = mark;
+    const int64_t start = a->start_pos[b], cur = len_at(kv, layer, s);
+    if (start != cur)
+      return fail(QL_ERR_INVALID,
+                  "positions[0] = %lld must continue from current_len (expected %lld); "
+                  "skipping, backward, or double writes are not allowed",
+                  (long long)start, (long long)cur);
+    if (start + n > kv->cfg.max_seq_len)
+      return fail(QL_ERR_INVALID, "positions[%lld] = %lld exceeds cache capacity %d",
+                  (long long)(kv->cfg.max_seq_len - start), (long long)kv->cfg.max_seq_len,
+                  kv->cfg.max_seq_len);
+    seqs[b] = s;
+    ends[b] = start + n;
+    st->seq[b] = s;
+    st->start[b] = static_cast<int32_t>(start);
+  }
+  QL_CUDA(cudaSetDevice(c->device), "set device");
+  bool patched = false;
+  int r = n > 0 ? reserve_pages(kv, seqs, ends, a->batch, &patched) : QL_OK;
+  if (r == QL_OK) r = ensure_rope(kv, a->rope_theta);
+  if (r != QL_OK) return r;
+  *view = view_of(kv, layer);
+  *rope = kv->d_rope;
+  return QL_OK;
+}
+
+void ql_kv_append_commit(ql_kv* kv, const ql_attn_args* a) {
+  for (int b = 0; b < a->batch; ++b)
+    len_at(kv, a->layer_idx, a->seq_ids[b]) = a->start_pos[b] + a->new_len;
+}
+
+extern "C" {
 
 int ql_attn_decode_noalloc(ql_ctx* c, ql_kv* kv, const ql_attn_args* a) {
   if (!c || !kv || !a) return fail(QL_ERR_INVALID, "ql_attn_decode_noalloc: NULL argument");

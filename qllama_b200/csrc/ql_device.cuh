@@ -21,6 +21,8 @@ enum : uint32_t {
   kStatusWaitTimeout = 1u,  // an mbarrier wait ran out of iterations
   kStatusBadPage = 2u,      // a block-table entry pointed outside the pool
   kStatusPeerTimeout = 4u,  // another GPU of a head-sharded call did not signal in time
+  kStatusBadLogits = 8u,    // the sampler met a non-finite logit
+  kStatusBadToken = 16u,    // a token id read on the device was outside the vocabulary
 };
 
 // Time bound for every spin on an mbarrier, in nanoseconds of %globaltimer:

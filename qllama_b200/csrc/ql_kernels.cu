@@ -24,6 +24,7 @@
 #include <atomic>
 #include <type_traits>
 
+#include "ql_append.cuh"
 #include "ql_device.cuh"
 #include "ql_kernels.cuh"
 
@@ -32,83 +33,6 @@ namespace ql {
 namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
-
-__device__ __forceinline__ int64_t cache_row(const CacheView& c, int seq, int pos, int h,
-                                             uint32_t* status, bool& ok) {
-  int page = c.block_table[static_cast<size_t>(seq) * c.pages_per_seq + pos / c.page];
-  if (page < 0 || page >= c.num_pages) {
-    ok = false;
-    if (status) atomicOr(status, kStatusBadPage);
-    return 0;
-  }
-  ok = true;
-  return (static_cast<int64_t>(page) * c.hkv + h) * c.page + pos % c.page;
-}
-
-// Source of the RoPE (cos, sin) pairs of one position: the host-built table
-// row, or (DEV) f64 pow/sincos evaluated on the device for callers that have
-// no table (the no-allocation decode entry point).
-struct RopeSrc {
-  const double2* row;  // table row of the position, or nullptr for "no rotation"
-  double pos;
-  double theta;
-};
-
-template <bool DEV>
-__device__ __forceinline__ double2 rope_cs(const RopeSrc& r, int p, int hd) {
-  if constexpr (DEV) {
-    const double f = pow(r.theta, -2.0 * static_cast<double>(p) / static_cast<double>(hd));
-    double sn, cs;
-    sincos(r.pos * f, &sn, &cs);
-    return make_double2(cs, sn);
-  } else {
-    return r.row[p];
-  }
-}
-
-// One warp writes one cache row (one position of one KV head): K rotated
-// by the table row when one is given, V as is, both converted to the cache
-// type.
-__device__ __forceinline__ void append_row(const void* kin, const void* vin, int in_dt,
-                                           size_t in_off, const double2* rope_row,
-                                           const CacheView& c, int64_t dst, int lane) {
-  const int hd = c.hd;
-  const int pairs = hd / 2;
-  const RopeSrc rope{rope_row, 0.0, 0.0};
-  for (int base = 0; base < pairs; base += 32) {
-    const int p = base + lane;
-    const bool valid = p < pairs;
-    float k0 = 0.f, k1 = 0.f, v0 = 0.f, v1 = 0.f;
-    if (valid) {
-      k0 = load_elem(kin, in_off + 2 * p, in_dt);
-      k1 = load_elem(kin, in_off + 2 * p + 1, in_dt);
-      v0 = load_elem(vin, in_off + 2 * p, in_dt);
-      v1 = load_elem(vin, in_off + 2 * p + 1, in_dt);
-      if (rope_row) rope_pair(k0, k1, rope_cs<false>(rope, p, hd), k0, k1);
-    }
-    const size_t e = static_cast<size_t>(dst) * hd + 2 * p;
-    if (c.dtype == kQ8_0) {
-      int8_t qk0, qk1, qv0, qv1;
-      __half sk, sv;
-      q8_0_pair(k0, k1, qk0, qk1, sk);
-      q8_0_pair(v0, v1, qv0, qv1, sv);
-      if (valid) {
-        *reinterpret_cast<char2*>(static_cast<int8_t*>(c.k) + e) = make_char2(qk0, qk1);
-        *reinterpret_cast<char2*>(static_cast<int8_t*>(c.v) + e) = make_char2(qv0, qv1);
-        if ((lane & 15) == 0) {
-          const size_t si = static_cast<size_t>(dst) * (hd / 32) + (2 * p) / 32;
-          c.k_scale[si] = __half_as_ushort(sk);
-          c.v_scale[si] = __half_as_ushort(sv);
-        }
-      }
-    } else if (valid) {
-      store_elem(c.k, e, c.dtype, k0);
-      store_elem(c.k, e + 1, c.dtype, k1);
-      store_elem(c.v, e, c.dtype, v0);
-      store_elem(c.v, e + 1, c.dtype, v1);
-    }
-  }
-}
 
 __device__ __forceinline__ float cache_value(const CacheView& c, const void* base,
                                              const uint16_t* scale, int64_t row, int d) {
@@ -126,19 +50,8 @@ __device__ __forceinline__ float cache_value(const CacheView& c, const void* bas
 __global__ void __launch_bounds__(128) append_kernel(const __grid_constant__ AppendArgs a) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const int hkv = a.cache.hkv;
-  const int rows = a.batch * a.new_len * hkv;
-  if (warp >= rows) return;
-  const int h = warp % hkv;
-  const int t = (warp / hkv) % a.new_len;
-  const int b = warp / (hkv * a.new_len);
-  const int pos = a.seqs.start[b] + t;
-  bool ok;
-  const int64_t dst = cache_row(a.cache, a.seqs.seq[b], pos, h, a.status, ok);
-  if (!ok) return;
-  const size_t in_off = (static_cast<size_t>(b * a.new_len + t) * hkv + h) * a.cache.hd;
-  const double2* rope = a.rope ? a.rope + static_cast<size_t>(pos) * (a.cache.hd / 2) : nullptr;
-  append_row(a.k, a.v, a.in_dtype, in_off, rope, a.cache, dst, lane);
+  if (warp >= a.batch * a.new_len * a.cache.hkv) return;
+  append_kv_row(a, warp, lane);
 }
 
 cudaError_t launch_append(const AppendArgs& a, cudaStream_t s) {
@@ -199,7 +112,7 @@ __global__ void __launch_bounds__(256) generic_kernel(const __grid_constant__ At
   extern __shared__ float sh[];  // q [hd], reduction [32]
   float* q = sh;
   float* red = sh + hd;
-  const double2* rope_row = a.rope + static_cast<size_t>(qpos) * (hd / 2);
+  const double2* rope_row = a.rope + static_cast<size_t>(qpos) * a.rope_stride;
   const size_t qoff = (static_cast<size_t>(job) * a.hq + h) * hd;
   for (int p = threadIdx.x; p < hd / 2; p += blockDim.x) {
     float y0, y1;
@@ -671,7 +584,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
              (static_cast<size_t>(job) * a.hq + kvh * a.group) * HD * ib;
       bytes = a.group * HD * ib;
     } else if (warp == 1 && !DEVROPE) {
-      base = reinterpret_cast<const char*>(a.rope + static_cast<size_t>(qpos) * (HD / 2));
+      base = reinterpret_cast<const char*>(a.rope + static_cast<size_t>(qpos) * a.rope_stride);
       bytes = HD / 2 * 16;
     } else if (warp >= 2 && appends) {
       base = static_cast<const char*>(warp == 2 ? a.k : a.v) + kv_off;
@@ -694,7 +607,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   if (a.peer.nranks && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
     peer_enter(a.peer, peer_epoch(a.peer));
 
-  const RopeSrc rsrc{DEVROPE ? nullptr : a.rope + static_cast<size_t>(qpos) * (HD / 2),
+  const RopeSrc rsrc{DEVROPE ? nullptr : a.rope + static_cast<size_t>(qpos) * a.rope_stride,
                      static_cast<double>(qpos), static_cast<double>(a.rope_theta)};
 
   // ------------------------------------------------------------ producer --

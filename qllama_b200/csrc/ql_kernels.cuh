@@ -89,6 +89,8 @@ struct AttnArgs {
   void* out;  // [batch, new_len, hq*hd]
   int32_t out_dtype;
   const double2* rope;
+  int32_t rope_stride;  // table entries per position: head_dim/2, or 0 (one identity row
+                        // for queries that arrive rotated)
   float rope_theta;  // used instead of `rope` by the device-RoPE variant
   CacheView cache;
   int32_t hq;
@@ -113,7 +115,7 @@ struct AttnArgs {
   SeqTable seqs;
 };
 
-// Multi-token causal attention on the tcgen05 tensor cores (f16 cache, hd 128).
+// Multi-token causal attention on the tcgen05 tensor cores (f16 cache, hd 64 or 128).
 struct PrefillArgs {
   const void* q;       // [batch, new_len, hq, hd] pre-RoPE
   int32_t in_dtype;
@@ -122,12 +124,14 @@ struct PrefillArgs {
   void* out;           // [batch, new_len, hq*hd]
   int32_t out_dtype;
   const double2* rope;
+  int32_t rope_stride;  // as in AttnArgs
   CacheView cache;
   int32_t hq;
   int32_t group;
   int32_t batch;
   int32_t new_len;
   float scale;
+  int32_t num_sms;     // SMs of the device (chooses one or two heads per CTA)
   uint32_t* status;
   SeqTable seqs;
 };
@@ -193,10 +197,13 @@ cudaError_t launch_gather(const GatherArgs& a, cudaStream_t s);
 cudaError_t launch_table_patch(const TablePatch& p, cudaStream_t s);
 
 // tcgen05 prefill: when it applies, rows of the rotated-q scratch it needs,
-// and the launch (rotated-q kernel, then the attention kernel).
+// and the launch: one prologue kernel (q rotated into the scratch, new K/V
+// rotated and appended into the cache as `ap` describes), then the attention
+// kernel.
 bool prefill_tc_supported(int hd, int dtype, int new_len);
 size_t prefill_q_rows(int new_len);
-cudaError_t launch_prefill_tc(const PrefillArgs& a, const CUtensorMap* qmap,
+cudaError_t launch_prefill_tc(const PrefillArgs& a, const AppendArgs& ap, const CUtensorMap* qmap,
                               const CUtensorMap* kmap, const CUtensorMap* vmap, cudaStream_t s);
+
 
 }  // namespace ql

@@ -13,7 +13,7 @@
 //               into a two-stage ring with separate K and V barriers; boxes of
 //               unallocated pages are read out of range, which TMA fills with
 //               zeros.
-//   warp 1      owns TMEM (512 columns) and issues every tcgen05.mma from one
+//   warp 1      owns TMEM (256 or 512 columns) and issues every tcgen05.mma from one
 //               thread: S_q(j) = Q_q K_j^T (A and B from shared memory) and
 //               O_q += P_q(j) V_j with P taken from TMEM; completion is
 //               signalled with tcgen05.commit on mbarriers.  The two heads'
@@ -31,6 +31,7 @@
 
 #include <atomic>
 
+#include "ql_append.cuh"
 #include "ql_device.cuh"
 #include "ql_kernels.cuh"
 
@@ -175,7 +176,8 @@ __device__ __forceinline__ float ex2_approx(float x) {  // 2^x; -inf -> +0
 
 // NQ query tiles (heads 2p, 2p+1 of one KV group when NQ == 2) share every
 // K/V tile.  TMEM columns: S_q at [128q, 128q+128) with P_q (f16 pairs)
-// written over its first 64 columns; O_q at [256 + 128q, 256 + 128q + HD).
+// written over its first 64 columns; O_q at [128NQ + 128q, 128NQ + 128q + HD):
+// 256 columns for one head (two CTAs can share an SM's TMEM), 512 for two.
 template <int HD, int NQ>
 struct PrefillCfg {
   static constexpr int kHalves = HD / 64;
@@ -187,8 +189,8 @@ struct PrefillCfg {
   static constexpr int kStageOff = kQOff + NQ * kQBytes;
   static constexpr int kBarOff = kStageOff + kStages * kStageBytes;
   static constexpr size_t kSmem = 1024 + kBarOff + 256;
-  static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kOCol = 256;
+  static constexpr uint32_t kTmemCols = NQ == 1 ? 256 : 512;
+  static constexpr uint32_t kOCol = 128 * NQ;
   static constexpr int kThreads = 128 * (1 + NQ);  // warpgroup 0: TMA + MMA; one per tile
 };
 
@@ -524,54 +526,70 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
   }
 }
 
-// ------------------------------------------------------ rotated-Q scratch --
-// One warp per (sequence, query row, query head), padding rows of the last
-// 128-row tile included (written as zeros): RoPE with the host table (bit
-// for bit the reference's rotation), rounded to f16, at
-// q_out[((b*hq + h)*q_rows + t)*hd + d].
-__global__ void __launch_bounds__(128) rope_q_kernel(const __grid_constant__ PrefillArgs a) {
+// -------------------------------------------------------------- prologue --
+// One launch before the attention kernel, one warp per row:
+//  * rows [0, q_rows_total): a query row (sequence, query row, head), padding
+//    rows of the last 128-row tile included (written as zeros): RoPE with the
+//    host table (bit for bit the reference's rotation), rounded to f16, at
+//    q_rot[((b*hq + h)*q_rows + t)*hd + d];
+//  * the rows after: a new K/V row (token, KV head): K rotated the same way,
+//    K and V converted and written into the cache (the append of
+//    layers.rs:397-413 / cache.rs:146-163).
+// Launched with programmatic dependent launch: everything it reads or writes
+// comes after the grid dependency wait, and the attention kernel's set-up
+// (barriers, TMEM, descriptors) overlaps this kernel.
+__global__ void __launch_bounds__(128) prefill_prologue_kernel(const __grid_constant__ PrefillArgs a,
+                                                               const __grid_constant__ AppendArgs ap) {
   const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const long long rows = static_cast<long long>(a.batch) * a.q_rows * a.hq;
-  if (w >= rows) return;
-  const int h = static_cast<int>(w % a.hq), t = static_cast<int>((w / a.hq) % a.q_rows);
-  const int b = static_cast<int>(w / (static_cast<long long>(a.hq) * a.q_rows));
+  griddep_wait();
+  griddep_launch_dependents();
+  const long long q_total = static_cast<long long>(a.batch) * a.q_rows * a.hq;
   const int hd = a.cache.hd;
-  __half* out = a.q_rot + ((static_cast<size_t>(b) * a.hq + h) * a.q_rows + t) * hd;
-  if (t >= a.new_len) {  // padding rows of the last query tile: zeros, never stale memory
-    for (int p = lane; p < hd / 2; p += 32)
-      *reinterpret_cast<__half2*>(out + 2 * p) = __floats2half2_rn(0.f, 0.f);
+  if (w < q_total) {
+    const int h = static_cast<int>(w % a.hq), t = static_cast<int>((w / a.hq) % a.q_rows);
+    const int b = static_cast<int>(w / (static_cast<long long>(a.hq) * a.q_rows));
+    __half* out = a.q_rot + ((static_cast<size_t>(b) * a.hq + h) * a.q_rows + t) * hd;
+    if (t >= a.new_len) {  // padding rows of the last query tile: zeros, never stale memory
+      for (int p = lane; p < hd / 2; p += 32)
+        *reinterpret_cast<__half2*>(out + 2 * p) = __floats2half2_rn(0.f, 0.f);
+      return;
+    }
+    const int pos = a.seqs.start[b] + t;
+    const double2* rr = a.rope + static_cast<size_t>(pos) * a.rope_stride;
+    const size_t in = (static_cast<size_t>(b * a.new_len + t) * a.hq + h) * hd;
+    for (int p = lane; p < hd / 2; p += 32) {
+      float y0, y1;
+      rope_pair(load_elem(a.q, in + 2 * p, a.in_dtype),
+                load_elem(a.q, in + 2 * p + 1, a.in_dtype), rr[p], y0, y1);
+      *reinterpret_cast<__half2*>(out + 2 * p) = __floats2half2_rn(y0, y1);
+    }
     return;
   }
-  const int pos = a.seqs.start[b] + t;
-  const double2* rr = a.rope + static_cast<size_t>(pos) * (hd / 2);
-  const size_t in = (static_cast<size_t>(b * a.new_len + t) * a.hq + h) * hd;
-  for (int p = lane; p < hd / 2; p += 32) {
-    float y0, y1;
-    rope_pair(load_elem(a.q, in + 2 * p, a.in_dtype), load_elem(a.q, in + 2 * p + 1, a.in_dtype),
-              rr[p], y0, y1);
-    *reinterpret_cast<__half2*>(out + 2 * p) = __floats2half2_rn(y0, y1);
-  }
+  const long long r = w - q_total;
+  const int hkv = a.cache.hkv;
+  if (r >= static_cast<long long>(ap.batch) * ap.new_len * hkv) return;
+  append_kv_row(ap, static_cast<int>(r), lane);
 }
 
 bool prefill_tc_supported(int hd, int dtype, int new_len) {
-  return hd == 128 && dtype == kF16 && new_len >= 64;
+  return (hd == 64 || hd == 128) && dtype == kF16 && new_len >= 64;
 }
 
 size_t prefill_q_rows(int new_len) { return static_cast<size_t>((new_len + kBM - 1) / kBM) * kBM; }
 
-template <int NQ>
+template <int HD, int NQ>
 static cudaError_t launch_prefill_nq(const PrefillArgs& a, const CUtensorMap* qmap,
                                      const CUtensorMap* kmap, const CUtensorMap* vmap,
                                      cudaStream_t s) {
-  using C = PrefillCfg<128, NQ>;
+  using C = PrefillCfg<HD, NQ>;
   constexpr int kMaxDev = 64;
   static std::atomic<bool> configured[kMaxDev];  // shared-memory limit set on that device
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= kMaxDev || !configured[dev].load(std::memory_order_acquire)) {
-    e = cudaFuncSetAttribute(prefill_tc_kernel<128, NQ>,
+    e = cudaFuncSetAttribute(prefill_tc_kernel<HD, NQ>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(C::kSmem));
     if (e != cudaSuccess) return e;
@@ -587,18 +605,39 @@ static cudaError_t launch_prefill_nq(const PrefillArgs& a, const CUtensorMap* qm
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, prefill_tc_kernel<128, NQ>, a, *qmap, *kmap, *vmap);
+  return cudaLaunchKernelEx(&cfg, prefill_tc_kernel<HD, NQ>, a, *qmap, *kmap, *vmap);
 }
 
-cudaError_t launch_prefill_tc(const PrefillArgs& a, const CUtensorMap* qmap,
+template <int HD>
+static cudaError_t launch_prefill_hd(const PrefillArgs& a, const CUtensorMap* qmap,
+                                     const CUtensorMap* kmap, const CUtensorMap* vmap,
+                                     cudaStream_t s) {
+  // Two heads of one KV group per CTA (one head's MMAs run while the other's
+  // softmax works) when the group has an even size and the grid still covers
+  // the SMs; a small call takes one head per CTA for twice the CTAs.
+  const long long tiles = (a.new_len + kBM - 1) / kBM;
+  const long long pair_ctas = tiles * (a.hq / 2) * a.batch;
+  if (a.group % 2 == 0 && pair_ctas >= a.num_sms) return launch_prefill_nq<HD, 2>(a, qmap, kmap, vmap, s);
+  return launch_prefill_nq<HD, 1>(a, qmap, kmap, vmap, s);
+}
+
+cudaError_t launch_prefill_tc(const PrefillArgs& a, const AppendArgs& ap, const CUtensorMap* qmap,
                               const CUtensorMap* kmap, const CUtensorMap* vmap, cudaStream_t s) {
-  const long long rows = static_cast<long long>(a.batch) * a.q_rows * a.hq;
-  rope_q_kernel<<<static_cast<unsigned>((rows + 3) / 4), 128, 0, s>>>(a);
-  cudaError_t e = cudaGetLastError();
+  const long long rows = static_cast<long long>(a.batch) * a.q_rows * a.hq +
+                         static_cast<long long>(ap.batch) * ap.new_len * ap.cache.hkv;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((rows + 3) / 4));
+  cfg.blockDim = dim3(128);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_prologue_kernel, a, ap);
   if (e != cudaSuccess) return e;
-  // Two heads of one KV group per CTA when the group has an even size.
-  if (a.group % 2 == 0) return launch_prefill_nq<2>(a, qmap, kmap, vmap, s);
-  return launch_prefill_nq<1>(a, qmap, kmap, vmap, s);
+  return a.cache.hd == 64 ? launch_prefill_hd<64>(a, qmap, kmap, vmap, s)
+                          : launch_prefill_hd<128>(a, qmap, kmap, vmap, s);
 }
 
 }  // namespace ql

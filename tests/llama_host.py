@@ -34,14 +34,8 @@ def linear(x: np.ndarray, w_out_in: np.ndarray) -> np.ndarray:
 
 
 def silu(x: np.ndarray) -> np.ndarray:
-    x = x.astype(np.float32)
-    with np.errstate(over="ignore"):
-        pos = x / (np.float32(1) + np.exp(-x))
-        e = np.exp(x)
-        neg = x * e / (np.float32(1) + e)
-    out = np.where(x >= 0, pos, neg).astype(np.float32)
-    out[x == -np.inf] = -0.0
-    return out
+    """ops.rs:222-239 through the oracle (libm expf, as Rust's f32::exp)."""
+    return oracle.silu(np.asarray(x, np.float32))
 
 
 class TinyModel:

@@ -11,7 +11,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def declared_symbols():
-    text = open(os.path.join(ROOT, "include", "qllama_attn.h")).read()
+    text = "".join(open(os.path.join(ROOT, "include", h)).read()
+                   for h in ("qllama_attn.h", "qllama_model.h"))
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
     return sorted(set(re.findall(r"\b(ql_[a-z0-9_]+)\s*\(", text)))
 

@@ -290,17 +290,22 @@ def test_long_context_q8_0_decode_sample(ctx):
                              gu.to_device(v, "bf16"), [L, L], hq, hkv, hd, theta)
 
 
-@pytest.mark.parametrize("batch,n,start,hq,hkv", [
-    (2, 200, 0, 8, 2),      # ragged last 128-row tile, GQA 4
-    (1, 512, 100, 16, 4),   # non-zero start: offset causal mask
-    (3, 128, 37, 4, 4),     # MHA, start inside a KV tile
-    (1, 1500, 0, 8, 8),     # many KV tiles: pipeline wrap, O rescaling
-    (1, 64, 0, 8, 1),       # one half-filled tile, GQA 8
+@pytest.mark.parametrize("batch,n,start,hq,hkv,hd", [
+    (2, 200, 0, 8, 2, 128),      # ragged last 128-row tile, GQA 4
+    (1, 512, 100, 16, 4, 128),   # non-zero start: offset causal mask
+    (3, 128, 37, 4, 4, 128),     # MHA, start inside a KV tile
+    (1, 1500, 0, 8, 8, 128),     # many KV tiles: pipeline wrap, O rescaling
+    (1, 64, 0, 8, 1, 128),       # one half-filled tile, GQA 8
+    (8, 1024, 0, 32, 8, 128),    # enough CTAs for two heads per CTA
+    (2, 200, 0, 8, 2, 64),       # head_dim 64: one 128-byte box per row
+    (1, 512, 100, 32, 4, 64),    # TinyLlama-shaped chunk at an offset
+    (1, 1500, 0, 8, 8, 64),
+    (4, 1024, 0, 32, 4, 64),     # two heads per CTA at head_dim 64
 ])
-def test_tcgen05_prefill_parity(ctx, batch, n, start, hq, hkv):
-    """Multi-token calls on an f16 cache with head_dim 128 run the tcgen05/TMEM kernel."""
-    rng = np.random.default_rng(n * 7 + start)
-    hd, theta = 128, 500000.0
+def test_tcgen05_prefill_parity(ctx, batch, n, start, hq, hkv, hd):
+    """Multi-token calls on an f16 cache with head_dim 64 or 128 run the tcgen05/TMEM kernel."""
+    rng = np.random.default_rng(n * 7 + start + hd)
+    theta = 500000.0
     p = gu.Pair(ctx, "f16", 1, start + n + 64, hkv, hd, batch)
     for s in range(batch):
         if start:
