@@ -39,9 +39,10 @@ calls).  The e2e steps also pay for page reservation: decode workloads keep
 going from where the previous step ended (sequences enter new pages as they
 grow) and whole jobs release their pages between steps (ql_kv_clear_seq).
 
-Multi-GPU (torchrun): the TinyLlama-shaped job splits its 4 KV heads over 2 or
-4 GPUs (strong scaling: outputs all-gathered over NVLink inside the kernels)
-and runs one replica per GPU on 8; times are the max over ranks.
+Multi-GPU (torchrun): the headline runs one replica of the TinyLlama-shaped
+job per GPU (weak scaling); "workloads" adds its head split over 2 or 4 GPUs
+(strong scaling, outputs all-gathered over NVLink inside the kernels) and the
+70B-shaped decode split over every GPU; times are the max over ranks.
 --impl reference times the CPU oracle (the restatement of the reference's Rust
 CPU attention) on this host's cores on a bounded sample of the same workload.
 """
@@ -64,11 +65,15 @@ sys.path.insert(0, ROOT)
 METRIC = "decode attn KV GB/s + prefill TFLOP/s (% roofline), tok/s at 1/2/4/8 B200"
 
 WORKLOADS = {
+    # shard_upto: the most GPUs the workload splits its KV heads over in the
+    # line's headline (0: replicas).  The batch-1 job is bound by per-call
+    # latency, which a per-layer exchange between GPUs only lengthens, so its
+    # headline runs one replica per GPU and its head split is reported beside it.
     "c2": dict(kind="job", unit="tok/s",
                desc="TinyLlama-1.1B-shaped attention: 22 layers, 32 Q / 4 KV heads, head_dim 64, "
                     "theta 1e4, f16 KV, batch 1, causal prefill 512 then 256 decode steps",
                layers=22, hq=32, hkv=4, hd=64, theta=10000.0, kv="f16", batch=1, prefill=512,
-               decode=256, in_dtype="f16", out_dtype="f16", page=64, shard_upto=4),
+               decode=256, in_dtype="f16", out_dtype="f16", page=64, shard_upto=0),
     "c3": dict(kind="decode", unit="GB/s",
                desc="Llama-2-7B-shaped MHA decode: 32 layers, 32/32 heads, head_dim 128, f16 KV "
                     "pre-filled to ragged lengths U[1024,4096], batch 16, 128 decode steps",
@@ -299,6 +304,9 @@ class Env:
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         torch.cuda.set_device(self.local)
         self.dev = torch.device("cuda", self.local)
+        # No NVLink multicast objects: the exchange uses plain peer stores, and
+        # NCCL's NVLS buffers are not needed for the gathers measured here.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         if self.world > 1:
             import datetime
 
@@ -453,9 +461,9 @@ def measure(env, name, w, steps, warmup, comm_mode="p2p", with_e2e=True):
 
     graphs = [(pname, capture(fn)) for pname, fn in phases]
     rewind()
-    counted = [graph_kernel_nodes(g) for _, g in graphs]
-    for _, g in graphs:
-        g.instantiate()
+    counted = [graph_kernel_nodes(gr) for _, gr in graphs]
+    for entry in graphs:
+        entry[1].instantiate()
     if all(c is not None for c in counted):
         launches, launch_src = sum(counted), "kernel nodes of the captured graphs"
     else:
@@ -467,8 +475,8 @@ def measure(env, name, w, steps, warmup, comm_mode="p2p", with_e2e=True):
 
     for _ in range(warmup):
         with torch.cuda.stream(stream):
-            for _, g in graphs:
-                g.replay()
+            for entry in graphs:
+                entry[1].replay()
     stream.synchronize()
     ctx.synchronize()
     nph = len(graphs)
@@ -481,8 +489,8 @@ def measure(env, name, w, steps, warmup, comm_mode="p2p", with_e2e=True):
         with torch.cuda.stream(stream):
             env.flush.zero_()  # evict the previous step's data from L2 (outside the events)
             ev[i][0].record(stream)
-            for p, (_, g) in enumerate(graphs):
-                g.replay()
+            for p, entry in enumerate(graphs):
+                entry[1].replay()
                 ev[i][p + 1].record(stream)
     env.barrier()
     clocks = sampler.stop()
@@ -491,7 +499,10 @@ def measure(env, name, w, steps, warmup, comm_mode="p2p", with_e2e=True):
     t_ph = env.max_over_ranks(t_ph)
     t_tot = sum(t_ph)
     ph = dict(zip([n for n, _ in graphs], t_ph))
-    del graphs  # released before the communicator (a graph may hold its NCCL calls)
+    # Every reference to the graphs goes before the communicator: a graph that
+    # holds NCCL calls keeps the communicator busy, and its destroy would wait.
+    del graphs, entry
+    torch.cuda.synchronize(dev)
 
     # ---- algorithmic work of one step (this rank's share)
     hbm, bf16, which = peaks()
@@ -694,7 +705,6 @@ def check_sharded(env, mode):
 
 def run_ours(args, w):
     env = Env()
-    torch = env.torch
     world, rank = env.world, env.rank
     steps, warmup = args.steps, args.warmup
     head = measure(env, args.workload, w, steps, warmup)
@@ -712,6 +722,12 @@ def run_ours(args, w):
                                                             "sample")}
                 extra[name] = r
         else:
+            # the head split of the north star's partition, beside the replicas:
+            # the TinyLlama-shaped job where its 4 KV heads divide the GPUs, and
+            # the 70B-shaped decode through the fused exchange and through NCCL
+            w2 = dict(WORKLOADS["c2"], shard_upto=4)
+            if sharded(w2, world):
+                extra["c2_heads"] = measure(env, "c2", w2, sub_steps, sub_warm)
             w5 = dict(WORKLOADS["c5"])
             if sharded(w5, world):
                 for mode in ("p2p", "nccl"):
@@ -759,8 +775,9 @@ def main():
                     help="override the workload's batch (a smaller case of the same shapes, "
                          "e.g. for an ncu capture; the line then names the changed config)")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count")
-    ap.add_argument("--shard", choices=("auto", "replicas"), default="auto",
-                    help="with several GPUs: the workload's own split (auto) or replicas")
+    ap.add_argument("--shard", choices=("auto", "heads", "replicas"), default="auto",
+                    help="with several GPUs: the workload's own choice (auto), its KV heads "
+                         "split over the GPUs, or replicas")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # at least three untimed steps
     w = dict(WORKLOADS[args.workload])
@@ -768,8 +785,8 @@ def main():
         if getattr(args, key) is not None:
             w[key] = getattr(args, key)
             w["desc"] += f" [{key} overridden to {w[key]}]"
-    if args.shard == "replicas":
-        w["shard_upto"] = 0
+    if args.shard != "auto":
+        w["shard_upto"] = 0 if args.shard == "replicas" else 8
     if args.impl == "reference":
         run_reference(args, w)
     else:

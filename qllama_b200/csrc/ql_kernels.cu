@@ -412,7 +412,8 @@ __device__ __forceinline__ bool peer_wait_entered(const PeerOut& po, uint32_t e,
   for (int p = 0; p < po.nranks && ok; ++p) ok = wait_epoch(po.flags[po.rank] + p, e, status);
   return ok;
 }
-// One thread per CTA, after the CTA's stores were fenced: counts the CTA.  The
+// One thread per CTA, after a CTA barrier that follows the CTA's stores:
+// fences them at system scope and counts the CTA.  The
 // last CTA of the launch tells every rank that this rank's stores are
 // visible, waits until every rank has told it the same (so the output is
 // complete when the kernel ends), re-arms the counter and records the call.
@@ -456,7 +457,8 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
         store8(po.out[p], off, a.out_dtype, res + hg * HD + d0, vec);
     }
   }
-  __threadfence_system();
+  // The barrier orders every thread's stores before thread 0's system fence
+  // in peer_arrive (a release is cumulative), so one fence covers the CTA.
   bar_consumers<NCT>();
   if (tid == 0) peer_arrive(po, e, a.status);
 }
@@ -1230,8 +1232,7 @@ __global__ void __launch_bounds__(256)
       }
     }
   }
-  __threadfence_system();
-  __syncthreads();
+  __syncthreads();  // thread 0's fence in peer_arrive then covers every thread's stores
   if (threadIdx.x == 0) peer_arrive(po, e, status);
 }
 

@@ -13,7 +13,7 @@
 //               into a two-stage ring with separate K and V barriers; boxes of
 //               unallocated pages are read out of range, which TMA fills with
 //               zeros.
-//   warp 1      owns TMEM (256 or 512 columns) and issues every tcgen05.mma from one
+//   warp 1      owns TMEM (512 columns) and issues every tcgen05.mma from one
 //               thread: S_q(j) = Q_q K_j^T (A and B from shared memory) and
 //               O_q += P_q(j) V_j with P taken from TMEM; completion is
 //               signalled with tcgen05.commit on mbarriers.  The two heads'
@@ -175,9 +175,11 @@ __device__ __forceinline__ float ex2_approx(float x) {  // 2^x; -inf -> +0
 }
 
 // NQ query tiles (heads 2p, 2p+1 of one KV group when NQ == 2) share every
-// K/V tile.  TMEM columns: S_q at [128q, 128q+128) with P_q (f16 pairs)
-// written over its first 64 columns; O_q at [128NQ + 128q, 128NQ + 128q + HD):
-// 256 columns for one head (two CTAs can share an SM's TMEM), 512 for two.
+// K/V tile.  TMEM columns: two S slots at [0, 128) and [128, 256), each with
+// its P (f16 pairs) written over its first 64 columns, and O_q at
+// [256 + 128q, 256 + 128q + HD).  Two heads: slot q holds head q's S.  One
+// head: the slots alternate between KV tiles (S(j) in slot j & 1), so the
+// next tile's S is computed while the softmax works on this one.
 template <int HD, int NQ>
 struct PrefillCfg {
   static constexpr int kHalves = HD / 64;
@@ -189,8 +191,8 @@ struct PrefillCfg {
   static constexpr int kStageOff = kQOff + NQ * kQBytes;
   static constexpr int kBarOff = kStageOff + kStages * kStageBytes;
   static constexpr size_t kSmem = 1024 + kBarOff + 256;
-  static constexpr uint32_t kTmemCols = NQ == 1 ? 256 : 512;
-  static constexpr uint32_t kOCol = 128 * NQ;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kOCol = 256;
   static constexpr int kThreads = 128 * (1 + NQ);  // warpgroup 0: TMA + MMA; one per tile
 };
 
@@ -228,9 +230,14 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
   uint64_t* k_empty = bars + 13;  // [2]
   uint64_t* v_full = bars + 15;   // [2]
   uint64_t* v_empty = bars + 17;  // [2]
-  uint64_t* s_full = bars + 5;    // [NQ] S_q(j) computed (and everything issued before it)
-  uint64_t* p_full = bars + 7;    // [NQ] P_q(j) written, O_q rescaled if needed
+  // One head per CTA (DB): the two S slots alternate between KV tiles, so
+  // s_full/p_full are per slot and the softmax waits for P(j-1).V through
+  // o_full before it rescales O.  Two heads: slot = head.
+  constexpr bool DB = NQ == 1;
+  uint64_t* s_full = bars + 5;    // [2] S of the slot computed (and everything issued before it)
+  uint64_t* p_full = bars + 7;    // [2] P of the slot written, O rescaled if needed
   uint64_t* o_done = bars + 9;    // all MMAs complete
+  uint64_t* o_full = bars + 19;   // DB: P(j).V complete, one phase per KV tile but the last
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -243,11 +250,12 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
     }
-    for (int q = 0; q < NQ; ++q) {
+    for (int q = 0; q < 2; ++q) {
       mbar_init(&s_full[q], 1);
       mbar_init(&p_full[q], 128);
     }
     mbar_init(o_done, 1);
+    mbar_init(o_full, 1);
     fence_mbar_init();
     tma_prefetch_desc(&qmap);
     tma_prefetch_desc(&kmap);
@@ -335,48 +343,79 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
       constexpr uint32_t idesc_o = instr_desc(kBM, HD, true);
       const uint32_t qaddr = smem_u32(qsm);
       bool ok = mbar_wait(q_full, 0, a.status);
-      auto issue_s = [&](int q, int j) {
+      // slot: the S/P columns (head q, or tile parity with one head)
+      auto issue_s = [&](int q, int slot, int j) {
         const uint32_t kaddr = smem_u32(stg + (j & 1) * C::kStageBytes);
 #pragma unroll
         for (int ks = 0; ks < HD / 16; ++ks) {
           const uint32_t koff = (ks >> 2) * (kBN * 128) + (ks & 3) * 32;
           const uint32_t qoff = q * C::kQBytes + (ks >> 2) * (kBM * 128) + (ks & 3) * 32;
-          tc_mma(tmem + q * kBN, smem_desc(qaddr + qoff, 16, 1024),
+          tc_mma(tmem + slot * kBN, smem_desc(qaddr + qoff, 16, 1024),
                  smem_desc(kaddr + koff, 16, 1024), idesc_s, ks > 0);
         }
-        tc_commit(&s_full[q]);
+        tc_commit(&s_full[slot]);
       };
-      auto issue_pv = [&](int q, int j) {
+      auto issue_pv = [&](int q, int slot, int j) {
         const uint32_t vaddr = smem_u32(stg + (j & 1) * C::kStageBytes + C::kKBytes);
 #pragma unroll
         for (int ks = 0; ks < kBN / 16; ++ks)
-          tc_mma_ts(tmem + C::kOCol + q * 128, tmem + q * kBN + ks * 8,
+          tc_mma_ts(tmem + C::kOCol + q * 128, tmem + slot * kBN + ks * 8,
                     smem_desc(vaddr + ks * 2048, kBN * 128, 1024), idesc_o, (j > 0 || ks > 0));
       };
-      for (int j = 0; ok && j < n_kv; ++j) {
-        ok = mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.status);
-        if (ok && j > 0) ok = mbar_wait(&v_full[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status);
-        if (!ok) break;
-        for (int q = 0; q < NQ; ++q) {
-          if (j > 0) {  // P_q(j-1) is in S_q's columns: consume it before S_q(j) overwrites them
-            if (!mbar_wait(&p_full[q], (j - 1) & 1, a.status)) {
-              ok = false;
-              break;
+      if constexpr (DB) {
+        // S(j) into slot j & 1 as soon as K(j) lands (the slot's P(j-2) was
+        // read by P(j-2).V, issued before it), then P(j-1).V once the
+        // softmax has written P(j-1): the tensor core runs S(j) while the
+        // softmax works on S(j-1).
+        for (int j = 0; ok && j < n_kv; ++j) {
+          ok = mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.status);
+          if (!ok) break;
+          tc_fence_after();
+          issue_s(0, j & 1, j);
+          tc_commit(&k_empty[j & 1]);
+          if (j > 0) {
+            ok = mbar_wait(&p_full[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status) &&
+                 mbar_wait(&v_full[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status);
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv(0, (j - 1) & 1, j - 1);
+            tc_commit(&v_empty[(j - 1) & 1]);
+            tc_commit(o_full);
+          }
+        }
+        const int last = n_kv - 1;
+        if (ok) ok = mbar_wait(&p_full[last & 1], (last >> 1) & 1, a.status) &&
+                     mbar_wait(&v_full[last & 1], (last >> 1) & 1, a.status);
+        if (ok) {
+          tc_fence_after();
+          issue_pv(0, last & 1, last);
+        }
+      } else {
+        for (int j = 0; ok && j < n_kv; ++j) {
+          ok = mbar_wait(&k_full[j & 1], (j >> 1) & 1, a.status);
+          if (ok && j > 0) ok = mbar_wait(&v_full[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status);
+          if (!ok) break;
+          for (int q = 0; q < NQ; ++q) {
+            if (j > 0) {  // P_q(j-1) is in S_q's columns: consume it before S_q(j) overwrites them
+              if (!mbar_wait(&p_full[q], (j - 1) & 1, a.status)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_pv(q, q, j - 1);
+              if (q == NQ - 1) tc_commit(&v_empty[(j - 1) & 1]);
             }
             tc_fence_after();
-            issue_pv(q, j - 1);
-            if (q == NQ - 1) tc_commit(&v_empty[(j - 1) & 1]);
+            issue_s(q, q, j);
           }
-          tc_fence_after();
-          issue_s(q, j);
+          if (ok) tc_commit(&k_empty[j & 1]);  // every S of tile j reads K(j) only
         }
-        if (ok) tc_commit(&k_empty[j & 1]);  // every S of tile j reads K(j) only
-      }
-      if (ok) ok = mbar_wait(&v_full[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, a.status);
-      for (int q = 0; ok && q < NQ; ++q) {
-        if (!mbar_wait(&p_full[q], (n_kv - 1) & 1, a.status)) break;
-        tc_fence_after();
-        issue_pv(q, n_kv - 1);
+        if (ok) ok = mbar_wait(&v_full[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, a.status);
+        for (int q = 0; ok && q < NQ; ++q) {
+          if (!mbar_wait(&p_full[q], (n_kv - 1) & 1, a.status)) break;
+          tc_fence_after();
+          issue_pv(q, q, n_kv - 1);
+        }
       }
       tc_commit(o_done);
     }
@@ -390,14 +429,17 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
     const int row = q_first + r;
     const int qpos = start + row;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
-    const uint32_t s_col = q * kBN, o_col = C::kOCol + q * 128;
+    const uint32_t o_col = C::kOCol + q * 128;
     const float sl2 = a.scale * kLog2eP;
     float m_used = -CUDART_INF_F, l = 0.f;
     // tcgen05.ld/st are warp-collective (.sync.aligned): every branch around
     // them below is taken by whole warps, decided with warp votes.
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[q], j & 1, a.status))) {
+      const int slot = DB ? (j & 1) : q;
+      const uint32_t s_col = slot * kBN;
+      const uint32_t s_par = DB ? ((j >> 1) & 1) : (j & 1);
+      if (!__all_sync(0xffffffffu, mbar_wait(&s_full[slot], s_par, a.status))) {
         ok = false;
         break;
       }
@@ -468,7 +510,14 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
         tmem_st16(lane_addr + s_col + c * 16, pk);
       }
       l = l * corr + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
-      if (rescale) {  // the previous P_q.V is complete: S_q(j) was issued after it
+      if (DB && rescale) {  // O is final only once P(j-1).V has completed
+        if (!__all_sync(0xffffffffu, mbar_wait(o_full, (j - 1) & 1, a.status))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      if (rescale) {  // two heads: the previous P_q.V is complete, S_q(j) was issued after it
 #pragma unroll
         for (int c = 0; c < HD / 32; ++c) {
           float v[32];
@@ -481,7 +530,7 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full[q]);
+      mbar_arrive(&p_full[slot]);
     }
     // ---- epilogue: O / l for the valid rows
     if (__all_sync(0xffffffffu, ok && mbar_wait(o_done, 0, a.status))) {
@@ -526,24 +575,9 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
   }
 }
 
-// -------------------------------------------------------------- prologue --
-// One launch before the attention kernel, one warp per row:
-//  * rows [0, q_rows_total): a query row (sequence, query row, head), padding
-//    rows of the last 128-row tile included (written as zeros): RoPE with the
-//    host table (bit for bit the reference's rotation), rounded to f16, at
-//    q_rot[((b*hq + h)*q_rows + t)*hd + d];
-//  * the rows after: a new K/V row (token, KV head): K rotated the same way,
-//    K and V converted and written into the cache (the append of
-//    layers.rs:397-413 / cache.rs:146-163).
-// Launched with programmatic dependent launch: everything it reads or writes
-// comes after the grid dependency wait, and the attention kernel's set-up
-// (barriers, TMEM, descriptors) overlaps this kernel.
-__global__ void __launch_bounds__(128) prefill_prologue_kernel(const __grid_constant__ PrefillArgs a,
-                                                               const __grid_constant__ AppendArgs ap) {
-  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  griddep_wait();
-  griddep_launch_dependents();
+// One row of the prologue: warp `w` of the grid (see prefill_prologue_kernel).
+__device__ __forceinline__ void prologue_row(const PrefillArgs& a, const AppendArgs& ap,
+                                             long long w, int lane) {
   const long long q_total = static_cast<long long>(a.batch) * a.q_rows * a.hq;
   const int hd = a.cache.hd;
   if (w < q_total) {
@@ -570,6 +604,30 @@ __global__ void __launch_bounds__(128) prefill_prologue_kernel(const __grid_cons
   const int hkv = a.cache.hkv;
   if (r >= static_cast<long long>(ap.batch) * ap.new_len * hkv) return;
   append_kv_row(ap, static_cast<int>(r), lane);
+}
+
+// -------------------------------------------------------------- prologue --
+// One launch before the attention kernel, one warp per row:
+//  * rows [0, q_rows_total): a query row (sequence, query row, head), padding
+//    rows of the last 128-row tile included (written as zeros): RoPE with the
+//    host table (bit for bit the reference's rotation), rounded to f16, at
+//    q_rot[((b*hq + h)*q_rows + t)*hd + d];
+//  * the rows after: a new K/V row (token, KV head): K rotated the same way,
+//    K and V converted and written into the cache (the append of
+//    layers.rs:397-413 / cache.rs:146-163).
+// Launched with programmatic dependent launch: everything it reads or writes
+// comes after the grid dependency wait.  Each block lets the attention kernel
+// launch only once its own rows are written: an attention CTA holds most of an
+// SM's registers while it waits, so releasing it early would starve the
+// prologue's remaining blocks; released at the end, its set-up (barriers,
+// TMEM, descriptors) overlaps the prologue's last wave.
+__global__ void __launch_bounds__(128) prefill_prologue_kernel(const __grid_constant__ PrefillArgs a,
+                                                               const __grid_constant__ AppendArgs ap) {
+  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  griddep_wait();
+  prologue_row(a, ap, w, lane);
+  griddep_launch_dependents();
 }
 
 bool prefill_tc_supported(int hd, int dtype, int new_len) {

@@ -290,6 +290,7 @@ def test_fused_projection_rope_append(ctx, storage, hd, hq, hkv, n):
                                     torch.from_numpy(k[None]).cuda(),
                                     torch.from_numpy(v[None]).cuda(), [start], hq, hkv, hd,
                                     theta, seq_ids=[b])
+        ctx.synchronize()  # the call ran on the context's stream
         assert torch.equal(twin[0], out[b])
     with pytest.raises(qb.QllamaError, match="must continue"):
         qm.qkv_rope_append(caches[0], 0, xt, wtt, start, hq, hkv, hd, theta)
