@@ -372,9 +372,13 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 // Bounded wait until the epoch counter *p reaches `epoch` (wrap-safe); raises
-// kStatusPeerTimeout and returns false after kPeerWaitLimitNs.
+// kStatusPeerTimeout and returns false after kPeerWaitLimitNs.  Once a wait of
+// the context has given up (the bit is set until the host reads it), later
+// waits return at once, so that a rank that left costs one wait limit, not
+// one per remaining call.
 __device__ __forceinline__ bool wait_epoch(const uint32_t* p, uint32_t epoch, uint32_t* status) {
   if (static_cast<int32_t>(ld_acquire_sys(p) - epoch) >= 0) return true;
+  if (status && (*reinterpret_cast<volatile uint32_t*>(status) & kStatusPeerTimeout)) return false;
   const uint64_t t0 = global_ns();
   for (;;) {
     for (int i = 0; i < 16; ++i) {

@@ -413,14 +413,19 @@ __device__ __forceinline__ bool peer_wait_entered(const PeerOut& po, uint32_t e,
   return ok;
 }
 // One thread per CTA, after a CTA barrier that follows the CTA's stores:
-// fences them at system scope and counts the CTA.  The
+// counts the CTA.  The
 // last CTA of the launch tells every rank that this rank's stores are
 // visible, waits until every rank has told it the same (so the output is
 // complete when the kernel ends), re-arms the counter and records the call.
+// Ordering without a system-wide fence: the CTA barrier before this call
+// orders the CTA's row stores (to this and the other GPUs) before this
+// thread's arrival; the arrival is a GPU-scope release/acquire add, so the
+// last CTA to arrive has every CTA's stores ordered before its own `done`
+// stores, which are system-scope releases; another GPU that reads `done` with
+// a system-scope acquire then sees the rows (release/acquire chains are
+// cumulative).
 __device__ __forceinline__ void peer_arrive(const PeerOut& po, uint32_t e, uint32_t* status) {
-  __threadfence_system();
-  if (atomicAdd(po.arrivals, 1) != po.total_ctas - 1) return;
-  __threadfence_system();
+  if (atom_add_acq_rel_gpu(po.arrivals, 1) != po.total_ctas - 1) return;
   for (int p = 0; p < po.nranks; ++p) st_release_sys(po.flags[p] + kMaxRanks + po.rank, e);
   bool ok = true;
   for (int p = 0; p < po.nranks && ok; ++p)
@@ -457,8 +462,8 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
         store8(po.out[p], off, a.out_dtype, res + hg * HD + d0, vec);
     }
   }
-  // The barrier orders every thread's stores before thread 0's system fence
-  // in peer_arrive (a release is cumulative), so one fence covers the CTA.
+  // The barrier orders every thread's stores before thread 0's arrival in
+  // peer_arrive, whose release covers them (a release is cumulative).
   bar_consumers<NCT>();
   if (tid == 0) peer_arrive(po, e, a.status);
 }
@@ -1232,7 +1237,7 @@ __global__ void __launch_bounds__(256)
       }
     }
   }
-  __syncthreads();  // thread 0's fence in peer_arrive then covers every thread's stores
+  __syncthreads();  // thread 0's release in peer_arrive then covers every thread's stores
   if (threadIdx.x == 0) peer_arrive(po, e, status);
 }
 
