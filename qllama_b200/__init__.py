@@ -13,6 +13,10 @@ for this path:
   heads split over several GPUs (one process each) and the outputs
   all-gathered into the reference's head-major layout (layers.rs:447-455).
 
+``qllama_b200.model`` holds the model host of include/qllama_model.h: the
+device ``Llama`` (Transformer, GGUF loading, generate), the device sampler and
+the fused Q/K/V projection.
+
 There is no CPU fallback: without the compiled library or a CUDA device the
 calls raise.
 """

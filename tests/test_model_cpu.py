@@ -120,3 +120,26 @@ def test_gguf_reader_validates_before_any_device_work(golden, tmp_path):
     mu.write_gguf(bad, t2, 3, 3, cfg["layers"], cfg["ff"], 128, cfg["eps"], cfg["theta"])
     assert "not divisible by attention.head_count" in _load(bad)[1]
     assert "cannot open" in _load(tmp_path / "missing.gguf")[1]
+    # string-array metadata (the token list) is skipped over, and its length
+    # must agree with the embedding's rows (config.rs:98-108)
+    for n_tokens, ok in ((cfg["vocab"], True), (cfg["vocab"] - 1, False)):
+        w = gguf.GGUFWriter(str(bad), "llama")
+        w.add_block_count(cfg["layers"])
+        w.add_context_length(128)
+        w.add_embedding_length(cfg["dim"])
+        w.add_feed_forward_length(cfg["ff"])
+        w.add_head_count(cfg["heads"])
+        w.add_head_count_kv(cfg["kv_heads"])
+        w.add_layer_norm_rms_eps(cfg["eps"])
+        w.add_token_list([f"tok{i}" for i in range(n_tokens)])
+        for name, a in t.items():
+            w.add_tensor(name, np.ascontiguousarray(a, np.float32))
+        w.write_header_to_file()
+        w.write_kv_data_to_file()
+        w.write_tensors_to_file()
+        w.close()
+        rc, msg = _load(bad)
+        if ok:
+            assert rc == qb.ERR_INVALID and "NULL context" in msg, msg
+        else:
+            assert "tokenizer.ggml.tokens has" in msg, msg
