@@ -15,7 +15,7 @@ random where the shape says "pre-filled"):
      128 decode steps of all 16 sequences through the 32 layers.  value: KV
      GB/s (algorithmic bytes read); tokens/s beside it.
   c4 Llama-3-8B-shaped GQA prefill: 32/8 heads, head_dim 128, theta 5e5, bf16
-     Q/K/V (f16 cache), 4 sequences x 8192 tokens; a step is one layer's causal
+     Q/K/V (bf16 cache), 4 sequences x 8192 tokens; a step is one layer's causal
      prefill.  value: TFLOP/s counting unmasked pairs only.
   c5 Llama-3-70B-shaped GQA decode: 64/8 heads, head_dim 128, Q8_0 KV of
      length 32768, 64 sequences; a step is 16 decode steps of one layer (80
@@ -82,8 +82,8 @@ WORKLOADS = {
                shard_upto=0),
     "c4": dict(kind="prefill", unit="TFLOP/s",
                desc="Llama-3-8B-shaped GQA causal prefill: 32/8 heads, head_dim 128, theta 5e5, "
-                    "bf16 Q/K/V, f16 KV, batch 4 x 8192 tokens, one layer",
-               layers=1, hq=32, hkv=8, hd=128, theta=500000.0, kv="f16", batch=4, prefill=8192,
+                    "bf16 Q/K/V, bf16 KV, batch 4 x 8192 tokens, one layer",
+               layers=1, hq=32, hkv=8, hd=128, theta=500000.0, kv="bf16", batch=4, prefill=8192,
                decode=0, in_dtype="bf16", out_dtype="bf16", page=64, shard_upto=0),
     "c5": dict(kind="decode", unit="GB/s",
                desc="Llama-3-70B-shaped GQA decode: 64/8 heads, head_dim 128, Q8_0 KV at length "
@@ -618,7 +618,9 @@ def measure(env, name, w, steps, warmup, comm_mode="p2p", with_e2e=True):
                 "frac": achieved / bf16, "peak_source": which,
                 "traffic": ncu_traffic(name, B, None) if not shard else None,
                 "flops_per_launch": pre_flops / Lyr, "launch_us": 1e6 * t_pre / Lyr,
-                "timed": "the whole call: append, rotated-q and attention kernels"}
+                "timed": "the whole call: append, rotated-q" +
+                         (", bf16-to-f16 tile conversion" if w["kv"] == "bf16" else "") +
+                         " and attention kernels"}
     else:
         t_dec = ph["decode"] / steps
         achieved = dec_bytes / t_dec / 1e9
@@ -775,13 +777,15 @@ def main():
                     help="override the workload's batch (a smaller case of the same shapes, "
                          "e.g. for an ncu capture; the line then names the changed config)")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count")
+    ap.add_argument("--kv", choices=("f32", "f16", "bf16", "q8_0"), default=None,
+                    help="override the KV cache storage type")
     ap.add_argument("--shard", choices=("auto", "heads", "replicas"), default="auto",
                     help="with several GPUs: the workload's own choice (auto), its KV heads "
                          "split over the GPUs, or replicas")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # at least three untimed steps
     w = dict(WORKLOADS[args.workload])
-    for key in ("batch", "layers"):
+    for key in ("batch", "layers", "kv"):
         if getattr(args, key) is not None:
             w[key] = getattr(args, key)
             w["desc"] += f" [{key} overridden to {w[key]}]"

@@ -955,7 +955,9 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
     tps = plan.tps;
     max_splits = plan.splits;
   }
-  // workspace: [staged q][k][v][out][part_o][part_ml][generic scratch f32][f64]
+  // workspace: [staged q][k][v][out][part_o][part_ml][rotated q][its row scales]
+  //            [bf16 caches: f16 copies of K and V, tile exponents]
+  //            [generic scratch f32][f64]
   size_t off = 0;
   const size_t o_q = off; off += align256(a->mem == QL_MEM_HOST ? qn * ib : 0);
   const size_t o_k = off; off += align256(a->mem == QL_MEM_HOST ? kn * ib : 0);
@@ -970,6 +972,18 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
   const size_t q_rows = ql::prefill_q_rows(n);
   const size_t o_qr = off;
   if (tc_prefill) off += align256(static_cast<size_t>(a->batch) * hq * q_rows * hd * 2);
+  const size_t o_qs = off;
+  if (tc_prefill) off += align256(static_cast<size_t>(a->batch) * hq * q_rows * sizeof(float));
+  // bf16: every key the call sees, per (sequence, KV head), padded to 128
+  const bool bf_copy = tc_prefill && kv->cfg.dtype == QL_BF16;
+  const size_t kv_rows = static_cast<size_t>((max_len + 127) / 128) * 128;
+  const size_t copy_bytes = static_cast<size_t>(a->batch) * hkv * kv_rows * hd * 2;
+  const size_t o_kc = off;
+  if (bf_copy) off += align256(copy_bytes);
+  const size_t o_vc = off;
+  if (bf_copy) off += align256(copy_bytes);
+  const size_t o_te = off;
+  if (bf_copy) off += align256(2 * static_cast<size_t>(a->batch) * hkv * (kv_rows / 128));
   const int gjobs = std::min(jobs, 65535);
   const size_t o_gs = off;
   if (!fast) off += align256(static_cast<size_t>(gjobs) * hq * max_len * sizeof(float));
@@ -1026,6 +1040,7 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
     pa.q = q;
     pa.in_dtype = a->in_dtype;
     pa.q_rot = reinterpret_cast<__half*>(w + o_qr);
+    pa.q_scale = reinterpret_cast<float*>(w + o_qs);
     pa.q_rows = static_cast<int32_t>(q_rows);
     pa.out = out;
     pa.out_dtype = a->out_dtype;
@@ -1043,7 +1058,22 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
     CUtensorMap qmap;
     r = encode_q_map(&qmap, w + o_qr, hd, static_cast<uint64_t>(a->batch) * hq * q_rows);
     if (r != QL_OK) return r;
-    QL_CUDA(ql::launch_prefill_tc(pa, ap, &qmap, &kv->kmap[layer], &kv->vmap[layer], c->stream),
+    const CUtensorMap* kmap = &kv->kmap[layer];
+    const CUtensorMap* vmap = &kv->vmap[layer];
+    CUtensorMap kcm, vcm;  // bf16: the attention kernel reads the f16 copies
+    if (bf_copy) {
+      pa.k_copy = reinterpret_cast<__half*>(w + o_kc);
+      pa.v_copy = reinterpret_cast<__half*>(w + o_vc);
+      pa.tile_exp = reinterpret_cast<int8_t*>(w + o_te);
+      pa.kv_rows = static_cast<int32_t>(kv_rows);
+      const uint64_t rows = static_cast<uint64_t>(a->batch) * hkv * kv_rows;
+      r = encode_map(&kcm, w + o_kc, QL_F16, hd, rows);
+      if (r == QL_OK) r = encode_map(&vcm, w + o_vc, QL_F16, hd, rows);
+      if (r != QL_OK) return r;
+      kmap = &kcm;
+      vmap = &vcm;
+    }
+    QL_CUDA(ql::launch_prefill_tc(pa, ap, &qmap, kmap, vmap, c->stream),
             "launch tcgen05 prefill");
     if (a->mem == QL_MEM_HOST) {
       QL_CUDA(cudaMemcpyAsync(a->out, out, qn * obb, cudaMemcpyDeviceToHost, c->stream),

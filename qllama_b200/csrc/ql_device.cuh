@@ -267,6 +267,21 @@ __device__ __forceinline__ void mma16832_s8(int (&d)[4], const uint4& a, uint32_
 }
 
 // -------------------------------------------------------------- elements --
+// f16 operand range of a block of values whose largest magnitude has the f32
+// bits `bits` (a non-negative value): the power of two 2^e to divide them by.
+// e = 0 while that magnitude lies in [2^-10, 2^15) (the values are used as
+// they are); otherwise e = floor(log2(magnitude)) - 14, which brings it into
+// [2^14, 2^15): below f16's overflow, and with small values kept off f16's
+// subnormal range.  Clamped to [-100, 113]; 0 for Inf/NaN (kept as they are).
+__device__ __forceinline__ int f16_range_exp(uint32_t bits) {
+  if (bits >= 0x7f800000u) return 0;
+  const int E = static_cast<int>(bits >> 23) - 127;
+  if (E >= -10 && E <= 14) return 0;
+  return E - 14 < -100 ? -100 : E - 14;
+}
+// 2^e as an f32, exactly, for -126 <= e <= 127.
+__device__ __forceinline__ float pow2f(int e) { return __int_as_float((127 + e) << 23); }
+
 template <bool BF>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   if constexpr (BF) {

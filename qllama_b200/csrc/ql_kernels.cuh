@@ -115,11 +115,12 @@ struct AttnArgs {
   SeqTable seqs;
 };
 
-// Multi-token causal attention on the tcgen05 tensor cores (f16 cache, hd 64 or 128).
+// Multi-token causal attention on the tcgen05 tensor cores (f16 or bf16 cache, hd 64 or 128).
 struct PrefillArgs {
   const void* q;       // [batch, new_len, hq, hd] pre-RoPE
   int32_t in_dtype;
-  __half* q_rot;       // scratch [batch][hq][q_rows][hd] f16, rotated q
+  __half* q_rot;       // scratch [batch][hq][q_rows][hd] f16, rotated q divided by q_scale
+  float* q_scale;      // scratch [batch][hq][q_rows]: 2^e per row, 1 unless |q| >= 2^15
   int32_t q_rows;      // new_len rounded up to the 128-row tile
   void* out;           // [batch, new_len, hq*hd]
   int32_t out_dtype;
@@ -134,6 +135,14 @@ struct PrefillArgs {
   int32_t num_sms;     // SMs of the device (chooses one or two heads per CTA)
   uint32_t* status;
   SeqTable seqs;
+  // bf16 caches: the keys the call sees, copied as f16 operands by a
+  // conversion pass into a dense scratch [batch][hkv][kv_rows][hd] (K, and V
+  // alike), each 128-key tile divided by 2^tile_exp; the attention kernel's
+  // tensor maps cover these copies.  tile_exp: [K, V][batch][hkv][kv_rows/128].
+  __half* k_copy;
+  __half* v_copy;
+  int8_t* tile_exp;
+  int32_t kv_rows;     // keys per (sequence, KV head) in the copies, a multiple of 128
 };
 
 struct GatherArgs {

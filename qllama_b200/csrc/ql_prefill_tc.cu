@@ -19,17 +19,25 @@
 //               signalled with tcgen05.commit on mbarriers.  The two heads'
 //               MMAs interleave, so one head's MMAs run while the other
 //               head's softmax warpgroup works.
+//   warps 2-3   bf16 caches only: convert each landed K/V tile to f16 in
+//               shared memory, scaled per tile by a power of two into f16's
+//               range (the MMAs wait for the converted tile).
 //   warps 4..   one softmax warpgroup per head, one thread per query row (=
 //               TMEM lane): read S (two passes of 32 columns: max, then
 //               exp2), write P as f16 pairs over S's first 64 columns; keep a
 //               running max that moves only when it grows by more than 2^8,
 //               rescaling that row of O in TMEM then; finally normalise O and
 //               store the output row.
-// Operands are f16 (cache f16, q rotated in f32 then rounded to f16); the
+// Operands are f16: the cache's f16 values, or its bf16 values times the
+// tile's power of two (exact for every value that f16 can hold at that
+// scale); q rotated in f32, divided by its row's power of two (1 unless the
+// row reaches 2^15) and rounded to f16.  Each power of two is folded back
+// into the scores or the output, so a bf16 cache keeps bf16's range.  The
 // accumulators are f32 in TMEM.  No cluster multicast is used anywhere.
 #include <math_constants.h>
 
 #include <atomic>
+#include <type_traits>
 
 #include "ql_append.cuh"
 #include "ql_device.cuh"
@@ -196,9 +204,26 @@ struct PrefillCfg {
   static constexpr int kThreads = 128 * (1 + NQ);  // warpgroup 0: TMA + MMA; one per tile
 };
 
+// bf16 -> f16 of two packed values, each times f (a power of two).
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w, float f) {
+  const __half2 h = __floats2half2_rn(__uint_as_float(w << 16) * f,
+                                      __uint_as_float(w & 0xffff0000u) * f);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// largest magnitude of eight packed bf16 values (NaN ignored, Inf kept)
+__device__ __forceinline__ float bf16x8_absmax(const uint4& w) {
+  const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    m = fmaxf(m, fmaxf(fabsf(__uint_as_float(in[i] << 16)),
+                       fabsf(__uint_as_float(in[i] & 0xffff0000u))));
+  return m;
+}
+
 }  // namespace
 
-template <int HD, int NQ>
+template <int HD, int NQ, bool BF>
 __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
     prefill_tc_kernel(const __grid_constant__ PrefillArgs a, const __grid_constant__ CUtensorMap qmap,
                       const __grid_constant__ CUtensorMap kmap,
@@ -294,7 +319,9 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
     for (int c0 = 0; c0 < 2 * n_kv && alive; c0 += 32) {
       const int u = c0 + lane, key0 = u * 64;
       int lane_row = oob_row;
-      if (u < 2 * n_kv && key0 / a.cache.page < a.cache.pages_per_seq) {
+      if (BF) {  // the dense f16 copy: rows of this (sequence, KV head) in key order
+        lane_row = (b * hkv + kvh) * a.kv_rows + key0;
+      } else if (u < 2 * n_kv && key0 / a.cache.page < a.cache.pages_per_seq) {
         const int page = __ldg(bt + key0 / a.cache.page);
         if (page >= 0 && page < a.cache.num_pages)
           lane_row = (page * hkv + kvh) * a.cache.page + key0 % a.cache.page;
@@ -430,7 +457,19 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
     const int qpos = start + row;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t o_col = C::kOCol + q * 128;
-    const float sl2 = a.scale * kLog2eP;
+    // The row's q was stored divided by its q_scale: the score scale puts it
+    // back.  bf16 caches: tile j's K arrives divided by 2^k_exp[j] (folded
+    // into that tile's score scale) and its V by 2^v_exp[j]; O accumulates
+    // P.V / 2^ev_used, ev_used the largest V exponent so far, so tile j's P
+    // is stored times 2^(v_exp[j] - ev_used) and O is rescaled when ev_used
+    // grows (the sum l stays in unscaled P).
+    const float sl2_row =
+        a.scale * kLog2eP * a.q_scale[(static_cast<size_t>(b) * a.hq + h) * a.q_rows + row];
+    int ev_used = -1000;  // set by the first tile
+    // bf16: this (sequence, KV head)'s tile exponents, K then V
+    const int8_t* tile_exp =
+        BF ? a.tile_exp + (static_cast<size_t>(b) * hkv + kvh) * (a.kv_rows / kBN) : nullptr;
+    const size_t v_exp_off = BF ? static_cast<size_t>(a.batch) * hkv * (a.kv_rows / kBN) : 0;
     float m_used = -CUDART_INF_F, l = 0.f;
     // tcgen05.ld/st are warp-collective (.sync.aligned): every branch around
     // them below is taken by whole warps, decided with warp votes.
@@ -444,8 +483,13 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
         break;
       }
       tc_fence_after();
+      float sl2 = sl2_row;
+      if constexpr (BF) {
+        const int ek = tile_exp[j];
+        if (ek) sl2 *= pow2f(ek);
+      }
       const int key0 = j * kBN;
-      if (q == 0 && j == n_kv - 1 && key0 + r >= kv_end &&
+      if (!BF && q == 0 && j == n_kv - 1 && key0 + r >= kv_end &&
           mbar_wait(&v_full[j & 1], (j >> 1) & 1, a.status)) {
         // Key r of the last tile lies past the sequence end: its V row may be
         // stale pool memory (Inf/NaN), and P = 0 times Inf would still reach
@@ -482,7 +526,7 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
       for (int i = 8; i < kBN; ++i) m8[i & 7] = fmaxf(m8[i & 7], x[i]);
       float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                        fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
-      mx *= sl2;
+      mx = __fmul_rn(mx, sl2);
       float corr = 1.f;
       bool rescale = false;
       if (mx > m_used + kRescaleLog2 || m_used == -CUDART_INF_F) {
@@ -494,22 +538,71 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
       // The warp rescales its O rows together; rows that kept their maximum
       // multiply by exactly 1.
       rescale = __any_sync(0xffffffffu, rescale);
-      // p = 2^(s*scale*log2e - m), packed f16 pairs over S's first 64 columns
+      // p = 2^(s*scale*log2e - m), packed f16 pairs over S's first 64 columns.
+      // m_used is the rounded product max(s)*scale*log2e; a fused multiply-add
+      // against it is off by up to half an ulp of that product, harmless
+      // below 2^20 but an overflow of 2^(...) for scores far above any
+      // attention's usual range, where the rounded products are subtracted
+      // instead (the largest then gives exactly 2^0).
       float ps[4] = {0.f, 0.f, 0.f, 0.f};
+      auto emit_p = [&](auto exact) {
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t pk[16];
+        for (int c = 0; c < kBN / 32; ++c) {
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = ex2_approx(fmaf(x[c * 32 + i], sl2, -m_used));
-          const float p1 = ex2_approx(fmaf(x[c * 32 + i + 1], sl2, -m_used));
-          ps[(i >> 1) & 3] += p0 + p1;
-          __half2 hp = __floats2half2_rn(p0, p1);
-          pk[i >> 1] = *reinterpret_cast<uint32_t*>(&hp);
+          for (int i = 0; i < 32; i += 2) {
+            float p0, p1;
+            if constexpr (decltype(exact)::value) {
+              // __fmul_rn: the product must be rounded on its own, not
+              // contracted into a multiply-add
+              p0 = ex2_approx(__fmul_rn(x[c * 32 + i], sl2) - m_used);
+              p1 = ex2_approx(__fmul_rn(x[c * 32 + i + 1], sl2) - m_used);
+            } else {
+              p0 = ex2_approx(fmaf(x[c * 32 + i], sl2, -m_used));
+              p1 = ex2_approx(fmaf(x[c * 32 + i + 1], sl2, -m_used));
+            }
+            ps[(i >> 1) & 3] += p0 + p1;
+            __half2 hp = __floats2half2_rn(p0, p1);
+            pk[i >> 1] = *reinterpret_cast<uint32_t*>(&hp);
+          }
+          tmem_st16(lane_addr + s_col + c * 16, pk);
         }
-        tmem_st16(lane_addr + s_col + c * 16, pk);
-      }
+      };
+      if (__any_sync(0xffffffffu, fabsf(m_used) >= 1048576.f))
+        emit_p(std::true_type{});
+      else
+        emit_p(std::false_type{});
       l = l * corr + ((ps[0] + ps[1]) + (ps[2] + ps[3]));
+      float ocorr = corr;  // O's factor
+      if constexpr (BF) {
+        // P(j) went out for ev == ev_used: a larger ev rescales O instead, a
+        // smaller one scales P(j) down (both rare: tiles of ordinary data all
+        // have exponent 0).
+        const int ev = tile_exp[v_exp_off + j];
+        if (ev > ev_used) {
+          if (j > 0) {
+            ocorr *= pow2f(ev_used - ev);
+            rescale = true;
+          }
+          ev_used = ev;
+        } else if (ev < ev_used) {
+          const float pf = pow2f(ev - ev_used);
+          tmem_wait_st();
+#pragma unroll
+          for (int c = 0; c < kBN / 64; ++c) {
+            float v[32];
+            tmem_ld32(lane_addr + s_col + c * 32, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&v[i]));
+              __half2 hp = __floats2half2_rn(f2.x * pf, f2.y * pf);
+              v[i] = *reinterpret_cast<const float*>(&hp);
+            }
+            tmem_st32(lane_addr + s_col + c * 32, v);
+          }
+        }
+      }
       if (DB && rescale) {  // O is final only once P(j-1).V has completed
         if (!__all_sync(0xffffffffu, mbar_wait(o_full, (j - 1) & 1, a.status))) {
           ok = false;
@@ -524,7 +617,7 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
           tmem_ld32(lane_addr + o_col + c * 32, v);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] *= corr;
+          for (int i = 0; i < 32; ++i) v[i] *= ocorr;
           tmem_st32(lane_addr + o_col + c * 32, v);
         }
       }
@@ -535,7 +628,7 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
     // ---- epilogue: O / l for the valid rows
     if (__all_sync(0xffffffffu, ok && mbar_wait(o_done, 0, a.status))) {
       tc_fence_after();
-      const float inv = 1.f / l;
+      const float inv = (BF ? pow2f(ev_used) : 1.f) / l;
       const size_t obase = ((static_cast<size_t>(b) * a.new_len + row) * a.hq + h) * HD;
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
@@ -583,21 +676,41 @@ __device__ __forceinline__ void prologue_row(const PrefillArgs& a, const AppendA
   if (w < q_total) {
     const int h = static_cast<int>(w % a.hq), t = static_cast<int>((w / a.hq) % a.q_rows);
     const int b = static_cast<int>(w / (static_cast<long long>(a.hq) * a.q_rows));
-    __half* out = a.q_rot + ((static_cast<size_t>(b) * a.hq + h) * a.q_rows + t) * hd;
+    const size_t qrow = (static_cast<size_t>(b) * a.hq + h) * a.q_rows + t;
+    __half* out = a.q_rot + qrow * hd;
     if (t >= a.new_len) {  // padding rows of the last query tile: zeros, never stale memory
       for (int p = lane; p < hd / 2; p += 32)
         *reinterpret_cast<__half2*>(out + 2 * p) = __floats2half2_rn(0.f, 0.f);
+      if (lane == 0) a.q_scale[qrow] = 1.f;
       return;
     }
     const int pos = a.seqs.start[b] + t;
     const double2* rr = a.rope + static_cast<size_t>(pos) * a.rope_stride;
     const size_t in = (static_cast<size_t>(b * a.new_len + t) * a.hq + h) * hd;
-    for (int p = lane; p < hd / 2; p += 32) {
-      float y0, y1;
-      rope_pair(load_elem(a.q, in + 2 * p, a.in_dtype),
-                load_elem(a.q, in + 2 * p + 1, a.in_dtype), rr[p], y0, y1);
-      *reinterpret_cast<__half2*>(out + 2 * p) = __floats2half2_rn(y0, y1);
+    // head_dim <= 128: at most two pairs per lane.  The row is stored divided
+    // by 2^e when its largest magnitude would not fit f16 (e = 0 otherwise,
+    // leaving the rounded values as they are); the attention kernel folds
+    // 2^e back into the row's score scale.
+    float y[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    float m = 0.f;
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int p = lane + 32 * it;
+      if (p < hd / 2) {
+        rope_pair(load_elem(a.q, in + 2 * p, a.in_dtype),
+                  load_elem(a.q, in + 2 * p + 1, a.in_dtype), rr[p], y[it][0], y[it][1]);
+        m = fmaxf(m, fmaxf(fabsf(y[it][0]), fabsf(y[it][1])));
+      }
     }
+    const int e = f16_range_exp(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
+    const float f = pow2f(-e);
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int p = lane + 32 * it;
+      if (p < hd / 2)
+        *reinterpret_cast<__half2*>(out + 2 * p) = __floats2half2_rn(y[it][0] * f, y[it][1] * f);
+    }
+    if (lane == 0) a.q_scale[qrow] = pow2f(e);
     return;
   }
   const long long r = w - q_total;
@@ -630,13 +743,77 @@ __global__ void __launch_bounds__(128) prefill_prologue_kernel(const __grid_cons
   griddep_launch_dependents();
 }
 
+// ------------------------------------------------------ bf16 conversion --
+// bf16 caches: one CTA per (128-key tile, K or V, KV head, sequence) copies
+// the keys the call sees into the dense f16 scratch, two threads per key row.
+// The tile is divided by 2^e, e = f16_range_exp of its largest magnitude (0
+// for ordinary data, where every bf16 value converts exactly, apart from
+// magnitudes under 2^-14 taking f16's subnormal spacing; otherwise the power
+// of two that puts the tile into [2^14, 2^15), exact for every value above
+// 2^(e-24)), and e goes to tile_exp for the attention kernel to fold back.
+// Keys past the sequence's end (and rows of unallocated pages) are zeros.
+// Converting once here, instead of in every attention CTA that reads the
+// tile, costs one read and one write of the keys (a few per cent of a long
+// prefill) and keeps the attention kernel's pipeline that of an f16 cache.
+template <int HD>
+__global__ void __launch_bounds__(256) bf16_tiles_to_f16_kernel(const __grid_constant__ PrefillArgs a) {
+  constexpr int kPer = HD / 16;  // 16-byte chunks per half row
+  const int tile = blockIdx.x, kind = blockIdx.y & 1, kvh = blockIdx.y >> 1, b = blockIdx.z;
+  const int hkv = a.cache.hkv;
+  const int kv_end = a.seqs.start[b] + a.new_len;
+  if (tile * kBN >= kv_end) return;  // never read
+  const int key = tile * kBN + (threadIdx.x >> 1), part = threadIdx.x & 1;
+  griddep_wait();
+  uint4 w[kPer];
+  bool live = key < kv_end;
+  if (live) {
+    const int page = a.cache.block_table[static_cast<size_t>(a.seqs.seq[b]) * a.cache.pages_per_seq +
+                                         key / a.cache.page];
+    live = page >= 0 && page < a.cache.num_pages;
+    if (live) {
+      const size_t row = (static_cast<size_t>(page) * hkv + kvh) * a.cache.page + key % a.cache.page;
+      const uint4* src = reinterpret_cast<const uint4*>(
+          static_cast<const uint16_t*>(kind ? a.cache.v : a.cache.k) + row * HD + part * (HD / 2));
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) w[i] = src[i];
+    }
+  }
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    if (!live) w[i] = make_uint4(0, 0, 0, 0);
+    m = fmaxf(m, bf16x8_absmax(w[i]));
+  }
+  __shared__ uint32_t wmax[8];
+  const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = mb;
+  __syncthreads();
+  uint32_t tb = wmax[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i) tb = max(tb, wmax[i]);
+  const int e = f16_range_exp(tb);
+  const float f = pow2f(-e);
+  const int kv_tiles = a.kv_rows / kBN;
+  if (threadIdx.x == 0)
+    a.tile_exp[((static_cast<size_t>(kind) * a.batch + b) * hkv + kvh) * kv_tiles + tile] =
+        static_cast<int8_t>(e);
+  uint4* dst = reinterpret_cast<uint4*>((kind ? a.v_copy : a.k_copy) +
+                                        ((static_cast<size_t>(b) * hkv + kvh) * a.kv_rows + key) * HD +
+                                        part * (HD / 2));
+#pragma unroll
+  for (int i = 0; i < kPer; ++i)
+    dst[i] = make_uint4(bf16x2_to_f16x2(w[i].x, f), bf16x2_to_f16x2(w[i].y, f),
+                        bf16x2_to_f16x2(w[i].z, f), bf16x2_to_f16x2(w[i].w, f));
+  griddep_launch_dependents();
+}
+
 bool prefill_tc_supported(int hd, int dtype, int new_len) {
-  return (hd == 64 || hd == 128) && dtype == kF16 && new_len >= 64;
+  return (hd == 64 || hd == 128) && (dtype == kF16 || dtype == kBF16) && new_len >= 64;
 }
 
 size_t prefill_q_rows(int new_len) { return static_cast<size_t>((new_len + kBM - 1) / kBM) * kBM; }
 
-template <int HD, int NQ>
+template <int HD, int NQ, bool BF>
 static cudaError_t launch_prefill_nq(const PrefillArgs& a, const CUtensorMap* qmap,
                                      const CUtensorMap* kmap, const CUtensorMap* vmap,
                                      cudaStream_t s) {
@@ -647,7 +824,7 @@ static cudaError_t launch_prefill_nq(const PrefillArgs& a, const CUtensorMap* qm
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev >= kMaxDev || !configured[dev].load(std::memory_order_acquire)) {
-    e = cudaFuncSetAttribute(prefill_tc_kernel<HD, NQ>,
+    e = cudaFuncSetAttribute(prefill_tc_kernel<HD, NQ, BF>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(C::kSmem));
     if (e != cudaSuccess) return e;
@@ -663,10 +840,10 @@ static cudaError_t launch_prefill_nq(const PrefillArgs& a, const CUtensorMap* qm
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, prefill_tc_kernel<HD, NQ>, a, *qmap, *kmap, *vmap);
+  return cudaLaunchKernelEx(&cfg, prefill_tc_kernel<HD, NQ, BF>, a, *qmap, *kmap, *vmap);
 }
 
-template <int HD>
+template <int HD, bool BF>
 static cudaError_t launch_prefill_hd(const PrefillArgs& a, const CUtensorMap* qmap,
                                      const CUtensorMap* kmap, const CUtensorMap* vmap,
                                      cudaStream_t s) {
@@ -675,8 +852,9 @@ static cudaError_t launch_prefill_hd(const PrefillArgs& a, const CUtensorMap* qm
   // the SMs; a small call takes one head per CTA for twice the CTAs.
   const long long tiles = (a.new_len + kBM - 1) / kBM;
   const long long pair_ctas = tiles * (a.hq / 2) * a.batch;
-  if (a.group % 2 == 0 && pair_ctas >= a.num_sms) return launch_prefill_nq<HD, 2>(a, qmap, kmap, vmap, s);
-  return launch_prefill_nq<HD, 1>(a, qmap, kmap, vmap, s);
+  if (a.group % 2 == 0 && pair_ctas >= a.num_sms)
+    return launch_prefill_nq<HD, 2, BF>(a, qmap, kmap, vmap, s);
+  return launch_prefill_nq<HD, 1, BF>(a, qmap, kmap, vmap, s);
 }
 
 cudaError_t launch_prefill_tc(const PrefillArgs& a, const AppendArgs& ap, const CUtensorMap* qmap,
@@ -708,8 +886,24 @@ cudaError_t launch_prefill_tc(const PrefillArgs& a, const AppendArgs& ap, const 
   cfg.numAttrs = fused ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_prologue_kernel, qa, fused ? ap : none);
   if (e != cudaSuccess) return e;
-  return a.cache.hd == 64 ? launch_prefill_hd<64>(a, qmap, kmap, vmap, s)
-                          : launch_prefill_hd<128>(a, qmap, kmap, vmap, s);
+  const bool bf = a.cache.dtype == kBF16;
+  if (bf) {  // the keys as f16 tiles, after the rows this call appends
+    cudaLaunchConfig_t cc = {};
+    cc.gridDim = dim3(static_cast<unsigned>(a.kv_rows / kBN), 2u * a.cache.hkv,
+                      static_cast<unsigned>(a.batch));
+    cc.blockDim = dim3(256);
+    cc.stream = s;
+    cc.attrs = attr;
+    cc.numAttrs = 1;
+    e = a.cache.hd == 64 ? cudaLaunchKernelEx(&cc, bf16_tiles_to_f16_kernel<64>, a)
+                         : cudaLaunchKernelEx(&cc, bf16_tiles_to_f16_kernel<128>, a);
+    if (e != cudaSuccess) return e;
+  }
+  if (a.cache.hd == 64)
+    return bf ? launch_prefill_hd<64, true>(a, qmap, kmap, vmap, s)
+              : launch_prefill_hd<64, false>(a, qmap, kmap, vmap, s);
+  return bf ? launch_prefill_hd<128, true>(a, qmap, kmap, vmap, s)
+            : launch_prefill_hd<128, false>(a, qmap, kmap, vmap, s);
 }
 
 }  // namespace ql

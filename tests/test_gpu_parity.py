@@ -290,6 +290,7 @@ def test_long_context_q8_0_decode_sample(ctx):
                              gu.to_device(v, "bf16"), [L, L], hq, hkv, hd, theta)
 
 
+@pytest.mark.parametrize("storage", ["f16", "bf16"])
 @pytest.mark.parametrize("batch,n,start,hq,hkv,hd", [
     (2, 200, 0, 8, 2, 128),      # ragged last 128-row tile, GQA 4
     (1, 512, 100, 16, 4, 128),   # non-zero start: offset causal mask
@@ -302,11 +303,12 @@ def test_long_context_q8_0_decode_sample(ctx):
     (1, 1500, 0, 8, 8, 64),
     (4, 1024, 0, 32, 4, 64),     # two heads per CTA at head_dim 64
 ])
-def test_tcgen05_prefill_parity(ctx, batch, n, start, hq, hkv, hd):
-    """Multi-token calls on an f16 cache with head_dim 64 or 128 run the tcgen05/TMEM kernel."""
+def test_tcgen05_prefill_parity(ctx, storage, batch, n, start, hq, hkv, hd):
+    """Multi-token calls on an f16 or bf16 cache with head_dim 64 or 128 run the
+    tcgen05/TMEM kernel (bf16 tiles converted to f16 operands in shared memory)."""
     rng = np.random.default_rng(n * 7 + start + hd)
     theta = 500000.0
-    p = gu.Pair(ctx, "f16", 1, start + n + 64, hkv, hd, batch)
+    p = gu.Pair(ctx, storage, 1, start + n + 64, hkv, hd, batch)
     for s in range(batch):
         if start:
             p.prefill_rows(rng, 0, s, start, theta)
@@ -328,19 +330,22 @@ def test_tcgen05_prefill_parity(ctx, batch, n, start, hq, hkv, hd):
     assert gu.max_err(out1, ref1) <= TOL_16
 
 
-def test_tcgen05_prefill_ignores_stale_rows_past_the_end(ctx):
+@pytest.mark.parametrize("storage", ["f16", "bf16"])
+def test_tcgen05_prefill_ignores_stale_rows_past_the_end(ctx, storage):
     """Pages keep old rows after a roll-back; keys past the end must not reach O.
 
-    Positions 0..255 are first written with Inf/NaN K and V and rolled back,
-    so the last 128-key tile of a 200-token prefill reads them (keys 200..255)
-    from the same pages. Their probabilities are exactly 0, and 0 * Inf must
-    not turn the visible rows into NaN."""
+    Positions 0..255 are first written with Inf/NaN K and V (and, in a bf16
+    cache, huge finite values) and rolled back, so the last 128-key tile of a
+    200-token prefill reads them (keys 200..255) from the same pages. Their
+    probabilities are exactly 0, and 0 * Inf must not turn the visible rows
+    into NaN; nor may their magnitudes set the f16 range of the tile's
+    operands."""
     rng = np.random.default_rng(23)
     hd, hq, hkv, theta, n = 128, 8, 2, 500000.0, 200
-    p = gu.Pair(ctx, "f16", 1, 320, hkv, hd, 1)
+    p = gu.Pair(ctx, storage, 1, 320, hkv, hd, 1)
     bad = np.full((256, hkv, hd), np.inf, np.float32)
     bad[:, :, 1::3] = np.nan
-    bad[:, :, 2::3] = -np.inf
+    bad[:, :, 2::3] = -np.inf if storage == "f16" else -1e30
     p.gpu.update(0, bad, bad, np.arange(256))
     p.gpu.truncate(0, 0)
     assert p.gpu.seq_len(0) == 0
@@ -358,6 +363,51 @@ def test_tcgen05_prefill_ignores_stale_rows_past_the_end(ctx):
     ref1 = p.oracle_forward(0, q1, k1, v1, [n], hq, theta)
     assert np.isfinite(out1.float().cpu().numpy()).all()
     assert gu.max_err(out1, ref1) <= TOL_16
+
+
+@pytest.mark.parametrize("scenario", ["small_q", "large_q"])
+@pytest.mark.parametrize("hd", [64, 128])
+def test_tcgen05_bf16_prefill_keeps_the_bf16_range(ctx, hd, scenario):
+    """A bf16 cache holds magnitudes far outside f16's; the tensor-core prefill
+    divides each K/V tile (and each rotated q row) by a power of two that puts
+    it in the f16 operand range and folds the factor back, so such values
+    neither overflow nor underflow nor disturb the other tiles.
+
+    small_q: q x 2^-16 everywhere, K of keys 128..255 x 2^16 (those scores stay
+    O(1)), V of keys 256..383 x 2^20, K of keys 384..511 and V of keys
+    512..599 x 2^-20.  large_q: q of every third token x 2^18 with all K
+    x 2^-18, V of keys 256..383 x 2^20.  Scores stay O(1) in both (large
+    scores would make the softmax an argmax, where any rounding of q picks
+    between near-ties)."""
+    rng = np.random.default_rng(hd + 3)
+    hq, hkv, theta, n = 8, 2, 500000.0, 600
+    p = gu.Pair(ctx, "bf16", 1, n + 64, hkv, hd, 1)
+    q = gu.normal(rng, (1, n, hq, hd))
+    k = gu.normal(rng, (1, n, hkv, hd))
+    v = gu.normal(rng, (1, n, hkv, hd))
+    if scenario == "small_q":
+        q *= 2.0 ** -16
+        k[:, 128:256] *= 2.0 ** 16
+        k[:, 384:512] *= 2.0 ** -20
+        v[:, 512:] *= 2.0 ** -20
+    else:
+        q[:, ::3] *= 2.0 ** 18
+        k *= 2.0 ** -18
+    v[:, 256:384] *= 2.0 ** 20
+    q, k, v = (gu.rounded(x, "bf16") for x in (q, k, v))
+    out = qb.attention_forward(p.gpu, 0, gu.to_device(q, "bf16"), gu.to_device(k, "bf16"),
+                               gu.to_device(v, "bf16"), [0], hq, hkv, hd, theta,
+                               out_dtype="f32")
+    p.gpu.ctx.synchronize()
+    ref = p.oracle_forward(0, q, k, v, [0], hq, theta)
+    got = out.float().cpu().numpy().reshape(ref.shape)
+    assert np.isfinite(got).all()
+    # 2e-3 of each token's output magnitude (at least 1): tokens that see the
+    # scaled V carry values near 2^20
+    err = np.abs(got.astype(np.float64) - ref).reshape(n, -1).max(axis=1)
+    mag = np.maximum(1.0, np.abs(ref).reshape(n, -1).max(axis=1))
+    assert (err / mag).max() <= TOL_16
+    assert err[:256].max() <= TOL_16  # before the scaled V: absolute
 
 
 def test_truncate_rolls_back_and_rewrites(ctx):

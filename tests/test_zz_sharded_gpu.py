@@ -25,6 +25,7 @@ pytestmark = [
 
 @pytest.mark.parametrize("storage,mode,prefill", [
     ("f16", "p2p", 130),   # tcgen05 prefill + push, then fused decodes
+    ("bf16", "p2p", 130),  # the same on a bf16 cache (tiles converted to f16 operands)
     ("q8_0", "p2p", 70),   # split-KV prefill + push, then fused decodes
     ("f16", "nccl", 130),  # the library baseline
 ])
