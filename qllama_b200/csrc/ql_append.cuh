@@ -86,6 +86,104 @@ __device__ __forceinline__ void append_row(const void* kin, const void* vin, int
   }
 }
 
+// N consecutive input elements (N = 2 or 4, i a multiple of N) as f32, in one
+// access when `vec` says the base is aligned to it, else one at a time.
+template <int N>
+__device__ __forceinline__ void load_vec(const void* base, size_t i, int dt, bool vec,
+                                         float (&x)[N]) {
+  static_assert(N == 2 || N == 4, "two or four elements");
+  if (!vec) {
+#pragma unroll
+    for (int k = 0; k < N; ++k) x[k] = load_elem(base, i + k, dt);
+    return;
+  }
+  if (dt == kF32) {
+    if constexpr (N == 4) {
+      const float4 v = *reinterpret_cast<const float4*>(static_cast<const float*>(base) + i);
+      x[0] = v.x, x[1] = v.y, x[2] = v.z, x[3] = v.w;
+    } else {
+      const float2 v = *reinterpret_cast<const float2*>(static_cast<const float*>(base) + i);
+      x[0] = v.x, x[1] = v.y;
+    }
+    return;
+  }
+  uint32_t w[N / 2];
+  if constexpr (N == 4) {
+    const uint2 v = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(base) + i);
+    w[0] = v.x, w[1] = v.y;
+  } else {
+    w[0] = *reinterpret_cast<const uint32_t*>(static_cast<const uint16_t*>(base) + i);
+  }
+#pragma unroll
+  for (int k = 0; k < N / 2; ++k) {
+    const float2 f = dt == kF16 ? __half22float2(*reinterpret_cast<const __half2*>(&w[k]))
+                                : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+    x[2 * k] = f.x, x[2 * k + 1] = f.y;
+  }
+}
+
+// N consecutive values into an f32, f16 or bf16 cache row at element i (a
+// multiple of N; cache rows are aligned), in one store.
+template <int N>
+__device__ __forceinline__ void store_vec(void* base, size_t i, int dt, const float (&x)[N]) {
+  if (dt == kF32) {
+    if constexpr (N == 4)
+      *reinterpret_cast<float4*>(static_cast<float*>(base) + i) = make_float4(x[0], x[1], x[2], x[3]);
+    else
+      *reinterpret_cast<float2*>(static_cast<float*>(base) + i) = make_float2(x[0], x[1]);
+    return;
+  }
+  uint32_t w[N / 2];
+#pragma unroll
+  for (int k = 0; k < N / 2; ++k)
+    w[k] = dt == kF16 ? pack2<false>(x[2 * k], x[2 * k + 1]) : pack2<true>(x[2 * k], x[2 * k + 1]);
+  if constexpr (N == 4)
+    *reinterpret_cast<uint2*>(static_cast<uint16_t*>(base) + i) = make_uint2(w[0], w[1]);
+  else
+    *reinterpret_cast<uint32_t*>(static_cast<uint16_t*>(base) + i) = w[0];
+}
+
+// One warp appends every KV head's row of one new token r (= b * new_len +
+// t) into an f32, f16 or bf16 cache with head_dim HD (64 or 128): the
+// position's page and (cos, sin) pairs are looked up once for all heads, and
+// each lane moves HD/32 consecutive values of a row.  Same rotation and
+// conversion as append_row.
+template <int HD>
+__device__ __forceinline__ void append_token(const AppendArgs& a, int r, int lane) {
+  constexpr int kN = HD / 32;  // values per lane: 2 or 4
+  const CacheView& c = a.cache;
+  const int b = r / a.new_len, t = r - b * a.new_len;
+  const int pos = a.seqs.start[b] + t;
+  const int page = c.block_table[static_cast<size_t>(a.seqs.seq[b]) * c.pages_per_seq + pos / c.page];
+  if (page < 0 || page >= c.num_pages) {
+    if (lane == 0 && a.status) atomicOr(a.status, kStatusBadPage);
+    return;
+  }
+  double2 cs[kN / 2];
+  if (a.rope) {
+#pragma unroll
+    for (int i = 0; i < kN / 2; ++i)
+      cs[i] = a.rope[static_cast<size_t>(pos) * (HD / 2) + lane * (kN / 2) + i];
+  }
+  const uintptr_t align = static_cast<uintptr_t>(kN) * (a.in_dtype == kF32 ? 4 : 2);
+  const bool kvec = reinterpret_cast<uintptr_t>(a.k) % align == 0;
+  const bool vvec = reinterpret_cast<uintptr_t>(a.v) % align == 0;
+  const size_t row0 = (static_cast<size_t>(page) * c.hkv) * c.page + pos % c.page;
+  for (int h = 0; h < c.hkv; ++h) {
+    const size_t in = (static_cast<size_t>(r) * c.hkv + h) * HD + kN * lane;
+    const size_t dst = (row0 + static_cast<size_t>(h) * c.page) * HD + kN * lane;
+    float k[kN], v[kN];
+    load_vec<kN>(a.k, in, a.in_dtype, kvec, k);
+    load_vec<kN>(a.v, in, a.in_dtype, vvec, v);
+    if (a.rope) {
+#pragma unroll
+      for (int i = 0; i < kN / 2; ++i) rope_pair(k[2 * i], k[2 * i + 1], cs[i], k[2 * i], k[2 * i + 1]);
+    }
+    store_vec<kN>(c.k, dst, c.dtype, k);
+    store_vec<kN>(c.v, dst, c.dtype, v);
+  }
+}
+
 __device__ __forceinline__ void append_kv_row(const AppendArgs& a, int warp, int lane) {
   const int hkv = a.cache.hkv;
   const int h = warp % hkv;

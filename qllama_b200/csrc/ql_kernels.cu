@@ -47,18 +47,33 @@ __device__ __forceinline__ float cache_value(const CacheView& c, const void* bas
 }  // namespace
 
 // ---------------------------------------------------------------- append --
+// TOKENS (head_dim 64 or 128, f32/f16/bf16 cache): one warp per new token,
+// every KV head's row (append_token); otherwise one warp per (token, KV head)
+// row (append_kv_row, which also quantises Q8_0 blocks).
+template <int TOKENS>
 __global__ void __launch_bounds__(128) append_kernel(const __grid_constant__ AppendArgs a) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (warp >= a.batch * a.new_len * a.cache.hkv) return;
-  append_kv_row(a, warp, lane);
+  if constexpr (TOKENS != 0) {
+    if (warp >= a.batch * a.new_len) return;
+    append_token<TOKENS>(a, warp, lane);
+  } else {
+    if (warp >= a.batch * a.new_len * a.cache.hkv) return;
+    append_kv_row(a, warp, lane);
+  }
 }
 
 cudaError_t launch_append(const AppendArgs& a, cudaStream_t s) {
-  const int rows = a.batch * a.new_len * a.cache.hkv;
-  if (rows == 0) return cudaSuccess;
-  const int blocks = (rows + 3) / 4;
-  append_kernel<<<blocks, 128, 0, s>>>(a);
+  const bool tokens = a.cache.dtype != kQ8_0 && (a.cache.hd == 64 || a.cache.hd == 128);
+  const int warps = a.batch * a.new_len * (tokens ? 1 : a.cache.hkv);
+  if (warps == 0) return cudaSuccess;
+  const int blocks = (warps + 3) / 4;
+  if (!tokens)
+    append_kernel<0><<<blocks, 128, 0, s>>>(a);
+  else if (a.cache.hd == 64)
+    append_kernel<64><<<blocks, 128, 0, s>>>(a);
+  else
+    append_kernel<128><<<blocks, 128, 0, s>>>(a);
   return cudaGetLastError();
 }
 

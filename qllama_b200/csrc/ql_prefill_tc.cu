@@ -668,66 +668,81 @@ __global__ void __launch_bounds__(PrefillCfg<HD, NQ>::kThreads, 1)
   }
 }
 
-// One row of the prologue: warp `w` of the grid (see prefill_prologue_kernel).
-__device__ __forceinline__ void prologue_row(const PrefillArgs& a, const AppendArgs& ap,
-                                             long long w, int lane) {
-  const long long q_total = static_cast<long long>(a.batch) * a.q_rows * a.hq;
-  const int hd = a.cache.hd;
-  if (w < q_total) {
-    const int h = static_cast<int>(w % a.hq), t = static_cast<int>((w / a.hq) % a.q_rows);
-    const int b = static_cast<int>(w / (static_cast<long long>(a.hq) * a.q_rows));
-    const size_t qrow = (static_cast<size_t>(b) * a.hq + h) * a.q_rows + t;
-    __half* out = a.q_rot + qrow * hd;
-    if (t >= a.new_len) {  // padding rows of the last query tile: zeros, never stale memory
-      for (int p = lane; p < hd / 2; p += 32)
-        *reinterpret_cast<__half2*>(out + 2 * p) = __floats2half2_rn(0.f, 0.f);
+// Query heads per prologue warp: the position's (cos, sin) pairs are read
+// once and serve every head of the group.
+constexpr int kQHeads = 4;
+
+// The rotated q rows of one (sequence, query row t, group of kQHeads heads),
+// warp-wide; padding rows of the last 128-row tile (t >= new_len) are written
+// as zeros, never left as stale memory.  Each lane moves HD/32 consecutive
+// values of a row.  A row is stored divided by 2^e, e = f16_range_exp of its
+// largest magnitude (0 for ordinary data, leaving the f16 rounding as it
+// was), and 2^e goes to q_scale for the attention kernel to fold into the
+// row's score scale.
+template <int HD>
+__device__ __forceinline__ void prologue_q(const PrefillArgs& a, int w, int lane) {
+  constexpr int kN = HD / 32;
+  const int ng = (a.hq + kQHeads - 1) / kQHeads;
+  const int g = w % ng, bt = w / ng;
+  const int t = bt % a.q_rows, b = bt / a.q_rows;
+  const int h0 = g * kQHeads, h1 = min(a.hq, h0 + kQHeads);
+  if (t >= a.new_len) {
+    for (int h = h0; h < h1; ++h) {
+      const size_t qrow = (static_cast<size_t>(b) * a.hq + h) * a.q_rows + t;
+      const float z[kN] = {};
+      store_vec<kN>(a.q_rot, qrow * HD + kN * lane, kF16, z);
       if (lane == 0) a.q_scale[qrow] = 1.f;
-      return;
     }
-    const int pos = a.seqs.start[b] + t;
-    const double2* rr = a.rope + static_cast<size_t>(pos) * a.rope_stride;
-    const size_t in = (static_cast<size_t>(b * a.new_len + t) * a.hq + h) * hd;
-    // head_dim <= 128: at most two pairs per lane.  The row is stored divided
-    // by 2^e when its largest magnitude would not fit f16 (e = 0 otherwise,
-    // leaving the rounded values as they are); the attention kernel folds
-    // 2^e back into the row's score scale.
-    float y[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    return;
+  }
+  const int pos = a.seqs.start[b] + t;
+  double2 cs[kN / 2];
+#pragma unroll
+  for (int i = 0; i < kN / 2; ++i)
+    cs[i] = a.rope[static_cast<size_t>(pos) * a.rope_stride + lane * (kN / 2) + i];
+  const bool vec =
+      reinterpret_cast<uintptr_t>(a.q) % (static_cast<uintptr_t>(kN) * (a.in_dtype == kF32 ? 4 : 2)) == 0;
+  for (int h = h0; h < h1; ++h) {
+    const size_t in = (static_cast<size_t>(b * a.new_len + t) * a.hq + h) * HD + kN * lane;
+    float y[kN];
+    load_vec<kN>(a.q, in, a.in_dtype, vec, y);
     float m = 0.f;
 #pragma unroll
-    for (int it = 0; it < 2; ++it) {
-      const int p = lane + 32 * it;
-      if (p < hd / 2) {
-        rope_pair(load_elem(a.q, in + 2 * p, a.in_dtype),
-                  load_elem(a.q, in + 2 * p + 1, a.in_dtype), rr[p], y[it][0], y[it][1]);
-        m = fmaxf(m, fmaxf(fabsf(y[it][0]), fabsf(y[it][1])));
-      }
+    for (int i = 0; i < kN / 2; ++i) {
+      rope_pair(y[2 * i], y[2 * i + 1], cs[i], y[2 * i], y[2 * i + 1]);
+      m = fmaxf(m, fmaxf(fabsf(y[2 * i]), fabsf(y[2 * i + 1])));
     }
     const int e = f16_range_exp(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
     const float f = pow2f(-e);
 #pragma unroll
-    for (int it = 0; it < 2; ++it) {
-      const int p = lane + 32 * it;
-      if (p < hd / 2)
-        *reinterpret_cast<__half2*>(out + 2 * p) = __floats2half2_rn(y[it][0] * f, y[it][1] * f);
-    }
+    for (int i = 0; i < kN; ++i) y[i] *= f;
+    const size_t qrow = (static_cast<size_t>(b) * a.hq + h) * a.q_rows + t;
+    store_vec<kN>(a.q_rot, qrow * HD + kN * lane, kF16, y);
     if (lane == 0) a.q_scale[qrow] = pow2f(e);
+  }
+}
+
+// Warp w of the prologue grid: first the q groups, then (fused calls) one
+// new token's K/V rows for every KV head.
+template <int HD>
+__device__ __forceinline__ void prologue_warp(const PrefillArgs& a, const AppendArgs& ap, int w,
+                                              int lane) {
+  const int q_warps = a.batch * a.q_rows * ((a.hq + kQHeads - 1) / kQHeads);
+  if (w < q_warps) {
+    prologue_q<HD>(a, w, lane);
     return;
   }
-  const long long r = w - q_total;
-  const int hkv = a.cache.hkv;
-  if (r >= static_cast<long long>(ap.batch) * ap.new_len * hkv) return;
-  append_kv_row(ap, static_cast<int>(r), lane);
+  const int r = w - q_warps;
+  if (r < ap.batch * ap.new_len) append_token<HD>(ap, r, lane);
 }
 
 // -------------------------------------------------------------- prologue --
-// One launch before the attention kernel, one warp per row:
-//  * rows [0, q_rows_total): a query row (sequence, query row, head), padding
-//    rows of the last 128-row tile included (written as zeros): RoPE with the
-//    host table (bit for bit the reference's rotation), rounded to f16, at
-//    q_rot[((b*hq + h)*q_rows + t)*hd + d];
-//  * the rows after: a new K/V row (token, KV head): K rotated the same way,
-//    K and V converted and written into the cache (the append of
-//    layers.rs:397-413 / cache.rs:146-163).
+// One launch before the attention kernel, one warp per (sequence, query row,
+// group of query heads), then, when the call's append is fused in, one warp
+// per new token: K rotated with the host table (bit for bit the reference's
+// rotation), K and V converted and written into the cache (the append of
+// layers.rs:397-413 / cache.rs:146-163); rotated q lands at
+// q_rot[((b*hq + h)*q_rows + t)*hd + d].
 // Launched with programmatic dependent launch: everything it reads or writes
 // comes after the grid dependency wait.  Each block lets the attention kernel
 // launch only once its own rows are written: an attention CTA holds most of an
@@ -736,10 +751,13 @@ __device__ __forceinline__ void prologue_row(const PrefillArgs& a, const AppendA
 // TMEM, descriptors) overlaps the prologue's last wave.
 __global__ void __launch_bounds__(128) prefill_prologue_kernel(const __grid_constant__ PrefillArgs a,
                                                                const __grid_constant__ AppendArgs ap) {
-  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int w = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
   griddep_wait();
-  prologue_row(a, ap, w, lane);
+  if (a.cache.hd == 64)
+    prologue_warp<64>(a, ap, w, lane);
+  else
+    prologue_warp<128>(a, ap, w, lane);
   griddep_launch_dependents();
 }
 
@@ -859,8 +877,8 @@ static cudaError_t launch_prefill_hd(const PrefillArgs& a, const CUtensorMap* qm
 
 cudaError_t launch_prefill_tc(const PrefillArgs& a, const AppendArgs& ap, const CUtensorMap* qmap,
                               const CUtensorMap* kmap, const CUtensorMap* vmap, cudaStream_t s) {
-  const long long q_rows = static_cast<long long>(a.batch) * a.q_rows * a.hq;
-  const long long kv_rows = static_cast<long long>(ap.batch) * ap.new_len * ap.cache.hkv;
+  const long long q_rows = static_cast<long long>(a.batch) * a.q_rows * ((a.hq + kQHeads - 1) / kQHeads);
+  const long long kv_rows = static_cast<long long>(ap.batch) * ap.new_len;
   // A call of a few waves of attention CTAs is bound by launch latency: one
   // prologue launch with programmatic dependent launch.  A large one keeps the
   // append and the rotation as two ordinary launches (measured a few per cent
