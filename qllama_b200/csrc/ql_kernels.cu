@@ -255,7 +255,7 @@ struct SplitCfg {
   static constexpr size_t kSmemCluster = smem_cluster(kMaxCluster);
   // warp partials [warps][8][HD], the output rows [8][HD], (max, sum) [8][2] and
   // the per-(warp, head) weights [warps][8], f32
-  static_assert(((kConsumerWarps + 1) * 8 * HD + 16 + 8 * kConsumerWarps) * 4 <=
+  static_assert(((kConsumerWarps + 1) * 8 * HD + 16 + 8 * kConsumerWarps + 16 * 8 + 64) * 4 <=
                     kStages * kStageBytes,
                 "merge buffer must fit the stages");
   static_assert(KG == 1 || (!kQ8 && kStages >= KG), "wide variant: f16/bf16, a stage per group");
@@ -1090,46 +1090,60 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     // A single GPU's output is stored from registers; a head-sharded call's
     // goes through emit_rows, which writes every rank's buffer in protocol.
     const bool direct = a.peer.nranks == 0;
-    // Unrolled over 8 or over the largest cluster with predicated loads, so
-    // that all the loads issue at once; splits past nsplit weigh 0.
+    // The LSE weights once per (split, head), not once per output column:
+    // thread t takes split t / 8 and head t % 8 (NCT = 128 covers 16 splits
+    // x 8 heads); each head's maximum and denominator are reduced over the
+    // splits a warp holds by shuffles, then over the four warps through
+    // shared memory (the stages are free by now).  Each thread then sums its
+    // four columns over the live splits with those weights.
+    // (Clusters run with one group of four consumer warps only: KG == 1.)
+    static_assert(KG > 1 || (NCT == 128 && C::kMaxCluster <= 16), "one thread per (split, head)");
+    float* mw = cml + 16;      // [16 splits][8 heads] weights
+    float* mh = mw + 16 * 8;   // [2][4 warps][8 heads]: maxima, then denominators
+    if constexpr (KG == 1) {
+      const int r = tid >> 3, hg = tid & 7, cw = tid >> 5;
+      const bool live = r < nsplit && hg < a.group;
+      const float m_r = live ? (r == 0 ? cml[2 * hg] : gml[r * 16 + 2 * hg]) : -CUDART_INF_F;
+      const float l_r = live ? (r == 0 ? cml[2 * hg + 1] : gml[r * 16 + 2 * hg + 1]) : 0.f;
+      float M = fmaxf(m_r, __shfl_xor_sync(0xffffffffu, m_r, 8));
+      M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 16));
+      if (lane < 8) mh[cw * 8 + lane] = M;
+      bar_consumers<NCT>();
+      M = fmaxf(fmaxf(mh[hg], mh[8 + hg]), fmaxf(mh[16 + hg], mh[24 + hg]));
+      const float w = live ? l_r * exp2f(m_r - (M == -CUDART_INF_F ? 0.f : M)) : 0.f;
+      mw[r * 8 + hg] = w;
+      float den = w + __shfl_xor_sync(0xffffffffu, w, 8);
+      den += __shfl_xor_sync(0xffffffffu, den, 16);
+      if (lane < 8) mh[32 + cw * 8 + lane] = den;
+      bar_consumers<NCT>();
+    }
     auto merge = [&](auto width) {
       constexpr int N = decltype(width)::value;
       for (int c = tid; c < a.group * (HD / 4); c += NCT) {
         const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
-        float mr[N], lr[N];
-        float M = -CUDART_INF_F;
+        const float den = (mh[32 + hg] + mh[40 + hg]) + (mh[48 + hg] + mh[56 + hg]);
+        // two accumulators halve the dependent chain of multiply-adds
+        float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
 #pragma unroll
         for (int r = 0; r < N; ++r) {
-          mr[r] = r == 0 ? cml[2 * hg] : (r < nsplit ? gml[r * 16 + 2 * hg] : -CUDART_INF_F);
-          lr[r] = r == 0 ? cml[2 * hg + 1] : (r < nsplit ? gml[r * 16 + 2 * hg + 1] : 0.f);
-          M = fmaxf(M, mr[r]);
-        }
-        const float Mb = M == -CUDART_INF_F ? 0.f : M;
-        float den = 0.f;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int r = 0; r < N; ++r) {
-          const float w = lr[r] * exp2f(mr[r] - Mb);
-          den += w;
-          const float4 v =
-              r == 0 ? *reinterpret_cast<const float4*>(res + hg * HD + d0)
-                     : (r < nsplit ? *reinterpret_cast<const float4*>(grows + (r * 8 + hg) * HD + d0)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f));
-          acc.x = fmaf(v.x, w, acc.x);
-          acc.y = fmaf(v.y, w, acc.y);
-          acc.z = fmaf(v.z, w, acc.z);
-          acc.w = fmaf(v.w, w, acc.w);
+          if (r >= nsplit) break;
+          const float w = mw[r * 8 + hg];
+          const float4 v = r == 0 ? *reinterpret_cast<const float4*>(res + hg * HD + d0)
+                                  : *reinterpret_cast<const float4*>(grows + (r * 8 + hg) * HD + d0);
+          float4& o = acc[r & 1];
+          o.x = fmaf(v.x, w, o.x);
+          o.y = fmaf(v.y, w, o.y);
+          o.z = fmaf(v.z, w, o.z);
+          o.w = fmaf(v.w, w, o.w);
         }
         const float inv = den > 0.f ? 1.f / den : 0.f;
-        acc.x *= inv;
-        acc.y *= inv;
-        acc.z *= inv;
-        acc.w *= inv;
+        const float4 out = make_float4((acc[0].x + acc[1].x) * inv, (acc[0].y + acc[1].y) * inv,
+                                       (acc[0].z + acc[1].z) * inv, (acc[0].w + acc[1].w) * inv);
         if (direct)
           store4(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d0,
-                 a.out_dtype, acc, a.out_vec != 0);
+                 a.out_dtype, out, a.out_vec != 0);
         else
-          *reinterpret_cast<float4*>(res + hg * HD + d0) = acc;
+          *reinterpret_cast<float4*>(res + hg * HD + d0) = out;
       }
     };
     if (C::kMaxCluster > 8 && nsplit > 8)
