@@ -724,7 +724,7 @@ def run_ours(args, w):
                                                             "sample")}
                 extra[name] = r
         else:
-            # the head split of the north star's partition, beside the replicas:
+            # the head split of the path's partition by KV heads, beside the replicas:
             # the TinyLlama-shaped job where its 4 KV heads divide the GPUs, and
             # the 70B-shaped decode through the fused exchange and through NCCL
             w2 = dict(WORKLOADS["c2"], shard_upto=4)
