@@ -974,8 +974,8 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
   if (tc_prefill) off += align256(static_cast<size_t>(a->batch) * hq * q_rows * hd * 2);
   const size_t o_qs = off;
   if (tc_prefill) off += align256(static_cast<size_t>(a->batch) * hq * q_rows * sizeof(float));
-  // bf16: every key the call sees, per (sequence, KV head), padded to 128
-  const bool bf_copy = tc_prefill && kv->cfg.dtype == QL_BF16;
+  // bf16 and Q8_0: every key the call sees, per (sequence, KV head), padded to 128
+  const bool bf_copy = tc_prefill && (kv->cfg.dtype == QL_BF16 || kv->cfg.dtype == QL_Q8_0);
   const size_t kv_rows = static_cast<size_t>((max_len + 127) / 128) * 128;
   const size_t copy_bytes = static_cast<size_t>(a->batch) * hkv * kv_rows * hd * 2;
   const size_t o_kc = off;
@@ -1060,7 +1060,7 @@ static int attn_forward_impl(ql_ctx* c, ql_kv* kv, const ql_attn_args* a,
     if (r != QL_OK) return r;
     const CUtensorMap* kmap = &kv->kmap[layer];
     const CUtensorMap* vmap = &kv->vmap[layer];
-    CUtensorMap kcm, vcm;  // bf16: the attention kernel reads the f16 copies
+    CUtensorMap kcm, vcm;  // bf16 / Q8_0: the attention kernel reads the f16 copies
     if (bf_copy) {
       pa.k_copy = reinterpret_cast<__half*>(w + o_kc);
       pa.v_copy = reinterpret_cast<__half*>(w + o_vc);

@@ -761,47 +761,77 @@ __global__ void __launch_bounds__(128) prefill_prologue_kernel(const __grid_cons
   griddep_launch_dependents();
 }
 
-// ------------------------------------------------------ bf16 conversion --
-// bf16 caches: one CTA per (128-key tile, K or V, KV head, sequence) copies
-// the keys the call sees into the dense f16 scratch, two threads per key row.
-// The tile is divided by 2^e, e = f16_range_exp of its largest magnitude (0
-// for ordinary data, where every bf16 value converts exactly, apart from
-// magnitudes under 2^-14 taking f16's subnormal spacing; otherwise the power
-// of two that puts the tile into [2^14, 2^15), exact for every value above
-// 2^(e-24)), and e goes to tile_exp for the attention kernel to fold back.
-// Keys past the sequence's end (and rows of unallocated pages) are zeros.
-// Converting once here, instead of in every attention CTA that reads the
-// tile, costs one read and one write of the keys (a few per cent of a long
-// prefill) and keeps the attention kernel's pipeline that of an f16 cache.
-template <int HD>
-__global__ void __launch_bounds__(256) bf16_tiles_to_f16_kernel(const __grid_constant__ PrefillArgs a) {
-  constexpr int kPer = HD / 16;  // 16-byte chunks per half row
+// ------------------------------------------------- f16 copy of the keys --
+// bf16 and Q8_0 caches: one CTA per (128-key tile, K or V, KV head,
+// sequence) copies the keys the call sees into the dense f16 scratch, two
+// threads per key row (each HD/2 values: bf16 as stored, Q8_0 dequantised
+// exactly in f32, int8 times its block's f16 scale).  The tile is divided by
+// 2^e, e = f16_range_exp of its largest magnitude (0 for ordinary data;
+// otherwise the power of two that puts the tile into [2^14, 2^15)), and e goes
+// to tile_exp for the attention kernel to fold back.  bf16 values convert
+// exactly at that scale, apart from magnitudes under 2^(e-24); dequantised
+// Q8_0 values (up to 19 significant bits) round to f16's 11.  Keys past the
+// sequence's end (and rows of unallocated pages) are zeros.  Converting once
+// here, instead of in every attention CTA that reads the tile, costs one read
+// and one write of the keys (a few per cent of a long prefill) and keeps the
+// attention kernel's pipeline that of an f16 cache.
+template <int HD, int DT>
+__global__ void __launch_bounds__(256) tiles_to_f16_kernel(const __grid_constant__ PrefillArgs a) {
+  static_assert(DT == kBF16 || DT == kQ8_0, "bf16 or Q8_0 storage");
+  constexpr int kVals = HD / 2;    // values per thread
+  constexpr int kPer = kVals / 8;  // 8-value groups per thread
   const int tile = blockIdx.x, kind = blockIdx.y & 1, kvh = blockIdx.y >> 1, b = blockIdx.z;
   const int hkv = a.cache.hkv;
   const int kv_end = a.seqs.start[b] + a.new_len;
   if (tile * kBN >= kv_end) return;  // never read
   const int key = tile * kBN + (threadIdx.x >> 1), part = threadIdx.x & 1;
   griddep_wait();
-  uint4 w[kPer];
+  float v[kVals];
   bool live = key < kv_end;
+  size_t row = 0;
   if (live) {
     const int page = a.cache.block_table[static_cast<size_t>(a.seqs.seq[b]) * a.cache.pages_per_seq +
                                          key / a.cache.page];
     live = page >= 0 && page < a.cache.num_pages;
-    if (live) {
-      const size_t row = (static_cast<size_t>(page) * hkv + kvh) * a.cache.page + key % a.cache.page;
-      const uint4* src = reinterpret_cast<const uint4*>(
-          static_cast<const uint16_t*>(kind ? a.cache.v : a.cache.k) + row * HD + part * (HD / 2));
+    row = (static_cast<size_t>(page) * hkv + kvh) * a.cache.page + key % a.cache.page;
+  }
+  if (!live) {
 #pragma unroll
-      for (int i = 0; i < kPer; ++i) w[i] = src[i];
+    for (int i = 0; i < kVals; ++i) v[i] = 0.f;
+  } else if constexpr (DT == kBF16) {
+    const uint4* src = reinterpret_cast<const uint4*>(
+        static_cast<const uint16_t*>(kind ? a.cache.v : a.cache.k) + row * HD + part * kVals);
+#pragma unroll
+    for (int g = 0; g < kPer; ++g) {
+      const uint4 w = src[g];
+      const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        v[8 * g + 2 * k] = __uint_as_float(in[k] << 16);
+        v[8 * g + 2 * k + 1] = __uint_as_float(in[k] & 0xffff0000u);
+      }
+    }
+  } else {
+    const uint4* src = reinterpret_cast<const uint4*>(
+        static_cast<const int8_t*>(kind ? a.cache.v : a.cache.k) + row * HD + part * kVals);
+    const uint16_t* sc = (kind ? a.cache.v_scale : a.cache.k_scale) + row * (HD / 32) +
+                         part * (kVals / 32);
+#pragma unroll
+    for (int q = 0; q < kVals / 16; ++q) {  // 16 int8 values per load
+      const uint4 w = src[q];
+      const float d = __half2float(__ushort_as_half(sc[q / 2]));  // 32-value blocks
+      const uint32_t in[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int byte = 0; byte < 4; ++byte)
+          v[16 * q + 4 * k + byte] =
+              static_cast<float>(static_cast<int8_t>((in[k] >> (8 * byte)) & 0xffu)) * d;
     }
   }
   float m = 0.f;
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    if (!live) w[i] = make_uint4(0, 0, 0, 0);
-    m = fmaxf(m, bf16x8_absmax(w[i]));
-  }
+  for (int i = 0; i < kVals; ++i) m = fmaxf(m, fabsf(v[i]));
   __shared__ uint32_t wmax[8];
   const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
   if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = mb;
@@ -817,16 +847,23 @@ __global__ void __launch_bounds__(256) bf16_tiles_to_f16_kernel(const __grid_con
         static_cast<int8_t>(e);
   uint4* dst = reinterpret_cast<uint4*>((kind ? a.v_copy : a.k_copy) +
                                         ((static_cast<size_t>(b) * hkv + kvh) * a.kv_rows + key) * HD +
-                                        part * (HD / 2));
+                                        part * kVals);
 #pragma unroll
-  for (int i = 0; i < kPer; ++i)
-    dst[i] = make_uint4(bf16x2_to_f16x2(w[i].x, f), bf16x2_to_f16x2(w[i].y, f),
-                        bf16x2_to_f16x2(w[i].z, f), bf16x2_to_f16x2(w[i].w, f));
+  for (int g = 0; g < kPer; ++g) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const __half2 h = __floats2half2_rn(v[8 * g + 2 * k] * f, v[8 * g + 2 * k + 1] * f);
+      w[k] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    dst[g] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
   griddep_launch_dependents();
 }
 
 bool prefill_tc_supported(int hd, int dtype, int new_len) {
-  return (hd == 64 || hd == 128) && (dtype == kF16 || dtype == kBF16) && new_len >= 64;
+  return (hd == 64 || hd == 128) && (dtype == kF16 || dtype == kBF16 || dtype == kQ8_0) &&
+         new_len >= 64;
 }
 
 size_t prefill_q_rows(int new_len) { return static_cast<size_t>((new_len + kBM - 1) / kBM) * kBM; }
@@ -884,7 +921,9 @@ cudaError_t launch_prefill_tc(const PrefillArgs& a, const AppendArgs& ap, const 
   // append and the rotation as two ordinary launches (measured a few per cent
   // faster on 4 x 8192 tokens, where their traffic, not their latency, counts).
   const long long ctas = static_cast<long long>((a.new_len + kBM - 1) / kBM) * a.hq * a.batch;
-  const bool fused = ctas < 8LL * a.num_sms;
+  // (append_token writes f32/f16/bf16 rows; a Q8_0 cache appends through
+  // append_kernel, which quantises its blocks)
+  const bool fused = ctas < 8LL * a.num_sms && a.cache.dtype != kQ8_0;
   PrefillArgs qa = a;
   AppendArgs none = ap;
   none.new_len = 0;
@@ -904,7 +943,7 @@ cudaError_t launch_prefill_tc(const PrefillArgs& a, const AppendArgs& ap, const 
   cfg.numAttrs = fused ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, prefill_prologue_kernel, qa, fused ? ap : none);
   if (e != cudaSuccess) return e;
-  const bool bf = a.cache.dtype == kBF16;
+  const bool bf = a.cache.dtype == kBF16 || a.cache.dtype == kQ8_0;  // reads the f16 copy
   if (bf) {  // the keys as f16 tiles, after the rows this call appends
     cudaLaunchConfig_t cc = {};
     cc.gridDim = dim3(static_cast<unsigned>(a.kv_rows / kBN), 2u * a.cache.hkv,
@@ -913,8 +952,13 @@ cudaError_t launch_prefill_tc(const PrefillArgs& a, const AppendArgs& ap, const 
     cc.stream = s;
     cc.attrs = attr;
     cc.numAttrs = 1;
-    e = a.cache.hd == 64 ? cudaLaunchKernelEx(&cc, bf16_tiles_to_f16_kernel<64>, a)
-                         : cudaLaunchKernelEx(&cc, bf16_tiles_to_f16_kernel<128>, a);
+    const bool q8 = a.cache.dtype == kQ8_0;
+    if (a.cache.hd == 64)
+      e = q8 ? cudaLaunchKernelEx(&cc, tiles_to_f16_kernel<64, kQ8_0>, a)
+             : cudaLaunchKernelEx(&cc, tiles_to_f16_kernel<64, kBF16>, a);
+    else
+      e = q8 ? cudaLaunchKernelEx(&cc, tiles_to_f16_kernel<128, kQ8_0>, a)
+             : cudaLaunchKernelEx(&cc, tiles_to_f16_kernel<128, kBF16>, a);
     if (e != cudaSuccess) return e;
   }
   if (a.cache.hd == 64)
