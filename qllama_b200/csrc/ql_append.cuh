@@ -169,18 +169,30 @@ __device__ __forceinline__ void append_token(const AppendArgs& a, int r, int lan
   const bool kvec = reinterpret_cast<uintptr_t>(a.k) % align == 0;
   const bool vvec = reinterpret_cast<uintptr_t>(a.v) % align == 0;
   const size_t row0 = (static_cast<size_t>(page) * c.hkv) * c.page + pos % c.page;
-  for (int h = 0; h < c.hkv; ++h) {
-    const size_t in = (static_cast<size_t>(r) * c.hkv + h) * HD + kN * lane;
-    const size_t dst = (row0 + static_cast<size_t>(h) * c.page) * HD + kN * lane;
-    float k[kN], v[kN];
-    load_vec<kN>(a.k, in, a.in_dtype, kvec, k);
-    load_vec<kN>(a.v, in, a.in_dtype, vvec, v);
-    if (a.rope) {
+  // kG heads' rows loaded before any is written: one memory round trip per
+  // group of heads, not one per head
+  constexpr int kG = 4;
+  for (int h0 = 0; h0 < c.hkv; h0 += kG) {
+    float k[kG][kN], v[kG][kN];
 #pragma unroll
-      for (int i = 0; i < kN / 2; ++i) rope_pair(k[2 * i], k[2 * i + 1], cs[i], k[2 * i], k[2 * i + 1]);
+    for (int g = 0; g < kG; ++g) {
+      if (h0 + g >= c.hkv) break;
+      const size_t in = (static_cast<size_t>(r) * c.hkv + h0 + g) * HD + kN * lane;
+      load_vec<kN>(a.k, in, a.in_dtype, kvec, k[g]);
+      load_vec<kN>(a.v, in, a.in_dtype, vvec, v[g]);
     }
-    store_vec<kN>(c.k, dst, c.dtype, k);
-    store_vec<kN>(c.v, dst, c.dtype, v);
+#pragma unroll
+    for (int g = 0; g < kG; ++g) {
+      if (h0 + g >= c.hkv) break;
+      if (a.rope) {
+#pragma unroll
+        for (int i = 0; i < kN / 2; ++i)
+          rope_pair(k[g][2 * i], k[g][2 * i + 1], cs[i], k[g][2 * i], k[g][2 * i + 1]);
+      }
+      const size_t dst = (row0 + static_cast<size_t>(h0 + g) * c.page) * HD + kN * lane;
+      store_vec<kN>(c.k, dst, c.dtype, k[g]);
+      store_vec<kN>(c.v, dst, c.dtype, v[g]);
+    }
   }
 }
 

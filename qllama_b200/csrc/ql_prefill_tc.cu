@@ -702,10 +702,19 @@ __device__ __forceinline__ void prologue_q(const PrefillArgs& a, int w, int lane
     cs[i] = a.rope[static_cast<size_t>(pos) * a.rope_stride + lane * (kN / 2) + i];
   const bool vec =
       reinterpret_cast<uintptr_t>(a.q) % (static_cast<uintptr_t>(kN) * (a.in_dtype == kF32 ? 4 : 2)) == 0;
-  for (int h = h0; h < h1; ++h) {
-    const size_t in = (static_cast<size_t>(b * a.new_len + t) * a.hq + h) * HD + kN * lane;
-    float y[kN];
-    load_vec<kN>(a.q, in, a.in_dtype, vec, y);
+  // every head's row first: one memory round trip for the group, not one per head
+  float ys[kQHeads][kN];
+#pragma unroll
+  for (int hh = 0; hh < kQHeads; ++hh) {
+    if (h0 + hh < h1)
+      load_vec<kN>(a.q, (static_cast<size_t>(b * a.new_len + t) * a.hq + h0 + hh) * HD + kN * lane,
+                   a.in_dtype, vec, ys[hh]);
+  }
+#pragma unroll
+  for (int hh = 0; hh < kQHeads; ++hh) {
+    const int h = h0 + hh;
+    if (h >= h1) break;
+    float* y = ys[hh];
     float m = 0.f;
 #pragma unroll
     for (int i = 0; i < kN / 2; ++i) {
@@ -714,10 +723,11 @@ __device__ __forceinline__ void prologue_q(const PrefillArgs& a, int w, int lane
     }
     const int e = f16_range_exp(__reduce_max_sync(0xffffffffu, __float_as_uint(m)));
     const float f = pow2f(-e);
+    float yo[kN];
 #pragma unroll
-    for (int i = 0; i < kN; ++i) y[i] *= f;
+    for (int i = 0; i < kN; ++i) yo[i] = y[i] * f;
     const size_t qrow = (static_cast<size_t>(b) * a.hq + h) * a.q_rows + t;
-    store_vec<kN>(a.q_rot, qrow * HD + kN * lane, kF16, y);
+    store_vec<kN>(a.q_rot, qrow * HD + kN * lane, kF16, yo);
     if (lane == 0) a.q_scale[qrow] = pow2f(e);
   }
 }
