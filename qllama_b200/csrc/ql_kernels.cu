@@ -485,7 +485,9 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
 
 }  // namespace
 
-template <int HD, int DT, bool DEVROPE, int KG>
+// CL: the launch is clustered (a.cluster > 1), a compile-time fact so that
+// each form holds only its own merge.
+template <int HD, int DT, bool DEVROPE, int KG, bool CL>
 __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, DT, KG>::kMinCtas)
     splitkv_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, int job0) {
@@ -516,7 +518,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   // Cluster mode: the splits of one (token, KV head) form a thread-block
   // cluster along x and merge through distributed shared memory; every CTA of
   // the cluster reaches both cluster barriers below on every path.
-  const bool cl = a.cluster > 1;
+  constexpr bool cl = CL;  // the host launches CL exactly when a.cluster > 1
   float* grows = reinterpret_cast<float*>(smem + C::kGatherOff);  // rank 0: [rank][8][HD]
   float* gml = grows + a.cluster * 8 * HD;                         // [rank][16] (max, sum)
   uint64_t* gbar = reinterpret_cast<uint64_t*>(gml + a.cluster * 16);  // counts their bytes
@@ -1329,17 +1331,22 @@ static cudaError_t configure_splitkv_t(int* ctas_per_sm) {
     if (ctas_per_sm) *ctas_per_sm = occupancy[dev].load(std::memory_order_relaxed);
     return cudaSuccess;
   }
-  e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE, KG>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(KG == 1 ? C::kSmemCluster : C::kSmem));
+  e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE, KG, false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmem));
   if (e != cudaSuccess) return e;
-  if (KG == 1 && C::kMaxCluster > 8) {
-    e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE, KG>,
-                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if constexpr (KG == 1) {  // clusters: the gather area too, and up to 16 CTAs
+    e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE, KG, true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(C::kSmemCluster));
     if (e != cudaSuccess) return e;
+    if (C::kMaxCluster > 8) {
+      e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE, KG, true>,
+                               cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return e;
+    }
   }
   int n = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, splitkv_kernel<HD, DT, DEVROPE, KG>,
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, splitkv_kernel<HD, DT, DEVROPE, KG, false>,
                                                     C::kThreads, C::kSmem);
   if (e != cudaSuccess) return e;
   n = max(n, 1);
@@ -1376,7 +1383,13 @@ static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    e = cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG>, a, *kmap, *vmap, j0);
+    if constexpr (KG == 1) {
+      e = a.cluster > 1
+              ? cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, true>, a, *kmap, *vmap, j0)
+              : cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, false>, a, *kmap, *vmap, j0);
+    } else {  // the wide variant never runs clustered
+      e = cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, false>, a, *kmap, *vmap, j0);
+    }
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
