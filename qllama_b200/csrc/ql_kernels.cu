@@ -452,12 +452,12 @@ __device__ __forceinline__ void peer_arrive(const PeerOut& po, uint32_t e, uint3
 // The 128 consumer threads write the group's output rows res[hg][0..HD): to
 // the call's output, or, for a head-sharded call, into every rank's output
 // (after every rank has entered the call), then count the CTA.
-template <int HD, int NCT>
+template <int HD, int NCT, bool PEER>
 __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, int job, int kvh,
                                           int tid, int* flag) {
   const PeerOut& po = a.peer;
   const bool vec = a.out_vec != 0;
-  if (po.nranks == 0) {
+  if (!PEER || po.nranks == 0) {
     for (int c = tid; c < a.group * (HD / 8); c += NCT) {
       const int hg = c / (HD / 8), d0 = (c % (HD / 8)) * 8;
       store8(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d0,
@@ -485,9 +485,11 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
 
 }  // namespace
 
-// CL: the launch is clustered (a.cluster > 1), a compile-time fact so that
-// each form holds only its own merge.
-template <int HD, int DT, bool DEVROPE, int KG, bool CL>
+// CL: the launch is clustered (a.cluster > 1); PEER: a head-sharded call
+// (a.peer.nranks > 0).  Compile-time facts, so that each form holds only its
+// own merge and exchange: the code a launch runs is fetched cold, and less of
+// it is faster.
+template <int HD, int DT, bool DEVROPE, int KG, bool CL, bool PEER>
 __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, DT, KG>::kMinCtas)
     splitkv_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, int job0) {
@@ -528,7 +530,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     // the bytes of the live splits only); it still arrives on the cluster
     // barrier that the others wait on.
     if (cl) cluster_arrive_relaxed();
-    if (a.peer.nranks) {  // still counted, once the previous call is done with the counters
+    if (PEER && a.peer.nranks) {  // still counted, once the previous call is done with the counters
       griddep_wait();
       if (threadIdx.x == 0) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
     }
@@ -628,7 +630,8 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   // A sharded call's number (*epoch + 1) is read where it is used rather than
   // kept live through the tile loop: no CTA stores the new count before every
   // CTA of the launch has arrived, and each CTA reads it before arriving.
-  if (a.peer.nranks && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
+  if (PEER && a.peer.nranks && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 &&
+      blockIdx.z == 0)
     peer_enter(a.peer, peer_epoch(a.peer));
 
   const RopeSrc rsrc{DEVROPE ? nullptr : a.rope + static_cast<size_t>(qpos) * a.rope_stride,
@@ -1078,7 +1081,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   }
   if (cl) {
     if (sender) {
-      if (tid == 0 && a.peer.nranks) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
+      if (PEER && tid == 0 && a.peer.nranks) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
       return;
     }
     // Rank 0 expects the bytes of every live split but itself (rows and
@@ -1091,7 +1094,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     mbar_wait_cluster(gbar, 0, a.status);
     // A single GPU's output is stored from registers; a head-sharded call's
     // goes through emit_rows, which writes every rank's buffer in protocol.
-    const bool direct = a.peer.nranks == 0;
+    const bool direct = !PEER || a.peer.nranks == 0;
     // The LSE weights once per (split, head), not once per output column:
     // thread t takes split t / 8 and head t % 8 (NCT = 128 covers 16 splits
     // x 8 heads); each head's maximum and denominator are reduced over the
@@ -1154,13 +1157,13 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
       merge(std::integral_constant<int, 8>{});
     if (!direct) {
       bar_consumers<NCT>();
-      emit_rows<HD, NCT>(a, res, job, kvh, tid, flag);
+      emit_rows<HD, NCT, PEER>(a, res, job, kvh, tid, flag);
     }
     return;
   }
   if (nsplit == 1) {
     bar_consumers<NCT>();
-    emit_rows<HD, NCT>(a, res, job, kvh, tid, flag);
+    emit_rows<HD, NCT, PEER>(a, res, job, kvh, tid, flag);
     return;
   }
   // ---- the last CTA of this (job, kv head) merges the splits
@@ -1175,7 +1178,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   }
   bar_consumers<NCT>();
   if (!flag[0]) {
-    if (a.peer.nranks && tid == 0) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
+    if (PEER && a.peer.nranks && tid == 0) peer_arrive(a.peer, peer_epoch(a.peer), a.status);
     return;
   }
   // Each thread sums four output columns over the splits with a running
@@ -1226,7 +1229,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   }
   if (tid == 0) a.counters[static_cast<size_t>(job) * hkv + kvh] = 0;
   bar_consumers<NCT>();
-  emit_rows<HD, NCT>(a, res, job, kvh, tid, flag);
+  emit_rows<HD, NCT, PEER>(a, res, job, kvh, tid, flag);
 }
 
 // ------------------------------------------------ head-sharded exchange --
@@ -1331,23 +1334,24 @@ static cudaError_t configure_splitkv_t(int* ctas_per_sm) {
     if (ctas_per_sm) *ctas_per_sm = occupancy[dev].load(std::memory_order_relaxed);
     return cudaSuccess;
   }
-  e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE, KG, false>,
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmem));
-  if (e != cudaSuccess) return e;
+  auto set_attrs = [](auto kernel, bool clustered) {
+    cudaError_t r = cudaFuncSetAttribute(
+        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        static_cast<int>(clustered ? C::kSmemCluster : C::kSmem));
+    if (r == cudaSuccess && clustered && C::kMaxCluster > 8)
+      r = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    return r;
+  };
+  e = set_attrs(splitkv_kernel<HD, DT, DEVROPE, KG, false, false>, false);
+  if (e == cudaSuccess) e = set_attrs(splitkv_kernel<HD, DT, DEVROPE, KG, false, true>, false);
   if constexpr (KG == 1) {  // clusters: the gather area too, and up to 16 CTAs
-    e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE, KG, true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(C::kSmemCluster));
-    if (e != cudaSuccess) return e;
-    if (C::kMaxCluster > 8) {
-      e = cudaFuncSetAttribute(splitkv_kernel<HD, DT, DEVROPE, KG, true>,
-                               cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-      if (e != cudaSuccess) return e;
-    }
+    if (e == cudaSuccess) e = set_attrs(splitkv_kernel<HD, DT, DEVROPE, KG, true, false>, true);
+    if (e == cudaSuccess) e = set_attrs(splitkv_kernel<HD, DT, DEVROPE, KG, true, true>, true);
   }
+  if (e != cudaSuccess) return e;
   int n = 0;
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, splitkv_kernel<HD, DT, DEVROPE, KG, false>,
-                                                    C::kThreads, C::kSmem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+      &n, splitkv_kernel<HD, DT, DEVROPE, KG, false, false>, C::kThreads, C::kSmem);
   if (e != cudaSuccess) return e;
   n = max(n, 1);
   if (dev < kMaxDev) occupancy[dev].store(n, std::memory_order_release);
@@ -1383,12 +1387,23 @@ static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
+    const bool peer = a.peer.nranks > 0;
     if constexpr (KG == 1) {
-      e = a.cluster > 1
-              ? cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, true>, a, *kmap, *vmap, j0)
-              : cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, false>, a, *kmap, *vmap, j0);
+      if (a.cluster > 1)
+        e = peer ? cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, true, true>, a,
+                                      *kmap, *vmap, j0)
+                 : cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, true, false>, a,
+                                      *kmap, *vmap, j0);
+      else
+        e = peer ? cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, false, true>, a,
+                                      *kmap, *vmap, j0)
+                 : cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, false, false>, a,
+                                      *kmap, *vmap, j0);
     } else {  // the wide variant never runs clustered
-      e = cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, false>, a, *kmap, *vmap, j0);
+      e = peer ? cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, false, true>, a,
+                                    *kmap, *vmap, j0)
+               : cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, false, false>, a,
+                                    *kmap, *vmap, j0);
     }
     if (e != cudaSuccess) return e;
   }
