@@ -281,20 +281,21 @@ __device__ __forceinline__ int q8_frag_byte(int h, int d, bool lo) {
 // loads first, then the converted row into shared memory and the release of
 // the consumers, then the same bytes into the cache.  Same conversion as
 // append_row_t; the cache is f16, bf16 or Q8_0 here.
-template <int HD, bool DEV>
+template <int HD, bool DEV, int IN = -1>
 __device__ __forceinline__ void append_fused(const AttnArgs& a, const RopeSrc& rope,
                                              size_t in_off, bool ok, int64_t dst, int lane,
                                              uint8_t* stage, uint64_t* released) {
+  const int in_dt = IN >= 0 ? IN : a.in_dtype;  // IN: the type known at compile time
   static_assert(HD % 64 == 0, "whole pairs per lane");
   constexpr int kIt = HD / 64;  // pairs per lane
-  const bool kvec = pair_aligned(a.k, a.in_dtype), vvec = pair_aligned(a.v, a.in_dtype);
+  const bool kvec = pair_aligned(a.k, in_dt), vvec = pair_aligned(a.v, in_dt);
   float2 kx[kIt], vx[kIt];
   double2 cs[kIt];
 #pragma unroll
   for (int it = 0; it < kIt; ++it) {
     const int p = it * 32 + lane;
-    kx[it] = load_pair(a.k, in_off + 2 * p, a.in_dtype, kvec);
-    vx[it] = load_pair(a.v, in_off + 2 * p, a.in_dtype, vvec);
+    kx[it] = load_pair(a.k, in_off + 2 * p, in_dt, kvec);
+    vx[it] = load_pair(a.v, in_off + 2 * p, in_dt, vvec);
     cs[it] = rope_cs<DEV>(rope, p, HD);
   }
 #pragma unroll
@@ -371,25 +372,26 @@ __device__ __forceinline__ void gather_q_pairs(int group, size_t row0, int tid, 
   }
 }
 
-template <int N, int NCT, int HD>
+template <int N, int NCT, int HD, int IN = -1>
 __device__ __forceinline__ void load_q_pairs(const AttnArgs& a, size_t row0, int tid,
                                              float2 (&x)[N]) {
   const void* q = a.q;
-  if (a.in_dtype == kF16 && pair_aligned(q, kF16)) {
+  const int in_dt = IN >= 0 ? IN : a.in_dtype;  // IN: the type known at compile time
+  if (in_dt == kF16 && pair_aligned(q, kF16)) {
     gather_q_pairs<N, NCT, HD>(a.group, row0, tid, x, [q](size_t i) {
       return __half22float2(*reinterpret_cast<const __half2*>(static_cast<const __half*>(q) + i));
     });
-  } else if (a.in_dtype == kBF16 && pair_aligned(q, kBF16)) {
+  } else if (in_dt == kBF16 && pair_aligned(q, kBF16)) {
     gather_q_pairs<N, NCT, HD>(a.group, row0, tid, x, [q](size_t i) {
       return __bfloat1622float2(
           *reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(q) + i));
     });
-  } else if (a.in_dtype == kF32 && pair_aligned(q, kF32)) {
+  } else if (in_dt == kF32 && pair_aligned(q, kF32)) {
     gather_q_pairs<N, NCT, HD>(a.group, row0, tid, x, [q](size_t i) {
       return *reinterpret_cast<const float2*>(static_cast<const float*>(q) + i);
     });
   } else {
-    const int dt = a.in_dtype;
+    const int dt = in_dt;
     gather_q_pairs<N, NCT, HD>(a.group, row0, tid, x, [q, dt](size_t i) {
       return make_float2(load_elem(q, i, dt), load_elem(q, i + 1, dt));
     });
@@ -452,16 +454,17 @@ __device__ __forceinline__ void peer_arrive(const PeerOut& po, uint32_t e, uint3
 // The 128 consumer threads write the group's output rows res[hg][0..HD): to
 // the call's output, or, for a head-sharded call, into every rank's output
 // (after every rank has entered the call), then count the CTA.
-template <int HD, int NCT, bool PEER>
+template <int HD, int NCT, bool PEER, int OUT = -1>
 __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, int job, int kvh,
                                           int tid, int* flag) {
   const PeerOut& po = a.peer;
   const bool vec = a.out_vec != 0;
+  const int out_dt = OUT >= 0 ? OUT : a.out_dtype;  // OUT: the type known at compile time
   if (!PEER || po.nranks == 0) {
     for (int c = tid; c < a.group * (HD / 8); c += NCT) {
       const int hg = c / (HD / 8), d0 = (c % (HD / 8)) * 8;
       store8(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d0,
-             a.out_dtype, res + hg * HD + d0, vec);
+             out_dt, res + hg * HD + d0, vec);
     }
     return;
   }
@@ -474,7 +477,7 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
       const size_t off =
           (static_cast<size_t>(job) * po.hq_total + po.head_base + kvh * a.group + hg) * HD + d0;
       for (int p = 0; p < po.nranks; ++p)
-        store8(po.out[p], off, a.out_dtype, res + hg * HD + d0, vec);
+        store8(po.out[p], off, out_dt, res + hg * HD + d0, vec);
     }
   }
   // The barrier orders every thread's stores before thread 0's arrival in
@@ -486,10 +489,11 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
 }  // namespace
 
 // CL: the launch is clustered (a.cluster > 1); PEER: a head-sharded call
-// (a.peer.nranks > 0).  Compile-time facts, so that each form holds only its
-// own merge and exchange: the code a launch runs is fetched cold, and less of
-// it is faster.
-template <int HD, int DT, bool DEVROPE, int KG, bool CL, bool PEER>
+// (a.peer.nranks > 0); IO: the input and output type when both are known
+// (-1: read from the arguments).  Compile-time facts, so that each form holds
+// only its own merge, exchange and conversions: the code a launch runs is
+// fetched cold, and less of it is faster.
+template <int HD, int DT, bool DEVROPE, int KG, bool CL, bool PEER, int IO>
 __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, DT, KG>::kMinCtas)
     splitkv_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, int job0) {
@@ -601,7 +605,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
       }
     }
   } else if (warp < 4) {
-    const int ib = a.in_dtype == kF32 ? 4 : 2;
+    const int ib = (IO >= 0 ? IO : a.in_dtype) == kF32 ? 4 : 2;
     const size_t kv_off = (static_cast<size_t>(job) * hkv + kvh) * HD * ib;
     const char* base = nullptr;
     int bytes = 0;
@@ -685,7 +689,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
       const int64_t dst =
           ok ? (static_cast<int64_t>(app_page) * hkv + kvh) * a.cache.page + qpos % a.cache.page
              : 0;
-      append_fused<HD, DEVROPE>(a, rsrc, (static_cast<size_t>(job) * hkv + kvh) * HD, ok, dst,
+      append_fused<HD, DEVROPE, IO>(a, rsrc, (static_cast<size_t>(job) * hkv + kvh) * HD, ok, dst,
                                 lane, newrow, appended);
       fence_proxy_async_global();
     };
@@ -729,7 +733,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     float* qmax = qfac + 8;                   // [8 heads][HD / 64 warps]
     float y[kIt][2];
     float2 xq[kIt];
-    load_q_pairs<kIt, NCT, HD>(a, qrow0, threadIdx.x, xq);
+    load_q_pairs<kIt, NCT, HD, IO>(a, qrow0, threadIdx.x, xq);
 #pragma unroll
     for (int it = 0; it < kIt; ++it) {
       const int idx = threadIdx.x + it * NCT, hg = idx / (HD / 2), p = idx % (HD / 2);
@@ -765,7 +769,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   } else {
     constexpr int kQIt = (8 * (HD / 2) + NCT - 1) / NCT;
     float2 xq[kQIt];
-    load_q_pairs<kQIt, NCT, HD>(a, qrow0, threadIdx.x, xq);
+    load_q_pairs<kQIt, NCT, HD, IO>(a, qrow0, threadIdx.x, xq);
 #pragma unroll
     for (int it = 0; it < kQIt; ++it) {
       const int idx = threadIdx.x + it * NCT, hg = idx / (HD / 2), p = idx % (HD / 2);
@@ -1146,7 +1150,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
                                        (acc[0].z + acc[1].z) * inv, (acc[0].w + acc[1].w) * inv);
         if (direct)
           store4(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d0,
-                 a.out_dtype, out, a.out_vec != 0);
+                 IO >= 0 ? IO : a.out_dtype, out, a.out_vec != 0);
         else
           *reinterpret_cast<float4*>(res + hg * HD + d0) = out;
       }
@@ -1157,13 +1161,13 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
       merge(std::integral_constant<int, 8>{});
     if (!direct) {
       bar_consumers<NCT>();
-      emit_rows<HD, NCT, PEER>(a, res, job, kvh, tid, flag);
+      emit_rows<HD, NCT, PEER, IO>(a, res, job, kvh, tid, flag);
     }
     return;
   }
   if (nsplit == 1) {
     bar_consumers<NCT>();
-    emit_rows<HD, NCT, PEER>(a, res, job, kvh, tid, flag);
+    emit_rows<HD, NCT, PEER, IO>(a, res, job, kvh, tid, flag);
     return;
   }
   // ---- the last CTA of this (job, kv head) merges the splits
@@ -1229,7 +1233,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   }
   if (tid == 0) a.counters[static_cast<size_t>(job) * hkv + kvh] = 0;
   bar_consumers<NCT>();
-  emit_rows<HD, NCT, PEER>(a, res, job, kvh, tid, flag);
+  emit_rows<HD, NCT, PEER, IO>(a, res, job, kvh, tid, flag);
 }
 
 // ------------------------------------------------ head-sharded exchange --
@@ -1322,6 +1326,25 @@ bool splitkv_supported(int hd, int dtype, int group, int page) {
 
 // Sets the kernel's shared-memory limit on the current device (once per
 // device) and reports how many of its CTAs an SM holds.
+using SplitKvFn = void (*)(const AttnArgs, const CUtensorMap, const CUtensorMap, int);
+
+// The compiled form for a launch: clustered or not, head-sharded or not, and
+// (single-GPU calls with the table's RoPE) I/O of the cache's own 16-bit type.
+template <int HD, int DT, bool DEVROPE, int KG>
+static SplitKvFn splitkv_form(bool clustered, bool peer, bool io) {
+  constexpr int kIO = DT == kQ8_0 ? -1 : DT;
+  if constexpr (KG == 1) {
+    if (clustered) {
+      if (peer) return splitkv_kernel<HD, DT, DEVROPE, KG, true, true, -1>;
+      if (io && !DEVROPE) return splitkv_kernel<HD, DT, DEVROPE, KG, true, false, kIO>;
+      return splitkv_kernel<HD, DT, DEVROPE, KG, true, false, -1>;
+    }
+  }
+  if (peer) return splitkv_kernel<HD, DT, DEVROPE, KG, false, true, -1>;
+  if (io && !DEVROPE) return splitkv_kernel<HD, DT, DEVROPE, KG, false, false, kIO>;
+  return splitkv_kernel<HD, DT, DEVROPE, KG, false, false, -1>;
+}
+
 template <int HD, int DT, bool DEVROPE, int KG>
 static cudaError_t configure_splitkv_t(int* ctas_per_sm) {
   using C = SplitCfg<HD, DT, KG>;
@@ -1334,24 +1357,21 @@ static cudaError_t configure_splitkv_t(int* ctas_per_sm) {
     if (ctas_per_sm) *ctas_per_sm = occupancy[dev].load(std::memory_order_relaxed);
     return cudaSuccess;
   }
-  auto set_attrs = [](auto kernel, bool clustered) {
-    cudaError_t r = cudaFuncSetAttribute(
-        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-        static_cast<int>(clustered ? C::kSmemCluster : C::kSmem));
-    if (r == cudaSuccess && clustered && C::kMaxCluster > 8)
-      r = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    return r;
-  };
-  e = set_attrs(splitkv_kernel<HD, DT, DEVROPE, KG, false, false>, false);
-  if (e == cudaSuccess) e = set_attrs(splitkv_kernel<HD, DT, DEVROPE, KG, false, true>, false);
-  if constexpr (KG == 1) {  // clusters: the gather area too, and up to 16 CTAs
-    if (e == cudaSuccess) e = set_attrs(splitkv_kernel<HD, DT, DEVROPE, KG, true, false>, true);
-    if (e == cudaSuccess) e = set_attrs(splitkv_kernel<HD, DT, DEVROPE, KG, true, true>, true);
+  // every compiled form: shared memory (clustered forms add the gather area)
+  // and, for clusters above 8 CTAs, the non-portable size
+  for (int form = 0; form < 8 && e == cudaSuccess; ++form) {
+    const bool clustered = form & 1, peer = form & 2, io = form & 4;
+    if (clustered && KG != 1) continue;
+    SplitKvFn k = splitkv_form<HD, DT, DEVROPE, KG>(clustered, peer, io);
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(clustered ? C::kSmemCluster : C::kSmem));
+    if (e == cudaSuccess && clustered && C::kMaxCluster > 8)
+      e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   }
   if (e != cudaSuccess) return e;
   int n = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-      &n, splitkv_kernel<HD, DT, DEVROPE, KG, false, false>, C::kThreads, C::kSmem);
+      &n, splitkv_form<HD, DT, DEVROPE, KG>(false, false, false), C::kThreads, C::kSmem);
   if (e != cudaSuccess) return e;
   n = max(n, 1);
   if (dev < kMaxDev) occupancy[dev].store(n, std::memory_order_release);
@@ -1365,6 +1385,9 @@ static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
   using C = SplitCfg<HD, DT, KG>;
   cudaError_t e = configure_splitkv_t<HD, DT, DEVROPE, KG>(nullptr);
   if (e != cudaSuccess) return e;
+  const bool io = DT != kQ8_0 && a.in_dtype == DT && a.out_dtype == DT;
+  const SplitKvFn kernel =
+      splitkv_form<HD, DT, DEVROPE, KG>(KG == 1 && a.cluster > 1, a.peer.nranks > 0, io);
   for (int j0 = 0; j0 < jobs; j0 += 65535) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.max_splits, a.cache.hkv, min(65535, jobs - j0));
@@ -1387,24 +1410,7 @@ static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
-    const bool peer = a.peer.nranks > 0;
-    if constexpr (KG == 1) {
-      if (a.cluster > 1)
-        e = peer ? cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, true, true>, a,
-                                      *kmap, *vmap, j0)
-                 : cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, true, false>, a,
-                                      *kmap, *vmap, j0);
-      else
-        e = peer ? cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, false, true>, a,
-                                      *kmap, *vmap, j0)
-                 : cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, false, false>, a,
-                                      *kmap, *vmap, j0);
-    } else {  // the wide variant never runs clustered
-      e = peer ? cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, false, true>, a,
-                                    *kmap, *vmap, j0)
-               : cudaLaunchKernelEx(&cfg, splitkv_kernel<HD, DT, DEVROPE, KG, false, false>, a,
-                                    *kmap, *vmap, j0);
-    }
+    e = cudaLaunchKernelEx(&cfg, kernel, a, *kmap, *vmap, j0);
     if (e != cudaSuccess) return e;
   }
   return cudaSuccess;
