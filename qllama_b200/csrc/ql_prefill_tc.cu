@@ -204,23 +204,6 @@ struct PrefillCfg {
   static constexpr int kThreads = 128 * (1 + NQ);  // warpgroup 0: TMA + MMA; one per tile
 };
 
-// bf16 -> f16 of two packed values, each times f (a power of two).
-__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w, float f) {
-  const __half2 h = __floats2half2_rn(__uint_as_float(w << 16) * f,
-                                      __uint_as_float(w & 0xffff0000u) * f);
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-// largest magnitude of eight packed bf16 values (NaN ignored, Inf kept)
-__device__ __forceinline__ float bf16x8_absmax(const uint4& w) {
-  const uint32_t in[4] = {w.x, w.y, w.z, w.w};
-  float m = 0.f;
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    m = fmaxf(m, fmaxf(fabsf(__uint_as_float(in[i] << 16)),
-                       fabsf(__uint_as_float(in[i] & 0xffff0000u))));
-  return m;
-}
-
 }  // namespace
 
 template <int HD, int NQ, bool BF>
