@@ -372,27 +372,28 @@ __device__ __forceinline__ void gather_q_pairs(int group, size_t row0, int tid, 
   }
 }
 
-template <int N, int NCT, int HD, int IN = -1>
+template <int N, int NCT, int HD, int IN = -1, int GRP = 0>
 __device__ __forceinline__ void load_q_pairs(const AttnArgs& a, size_t row0, int tid,
                                              float2 (&x)[N]) {
   const void* q = a.q;
+  const int gsize = GRP ? GRP : a.group;  // GRP: the group size known at compile time
   const int in_dt = IN >= 0 ? IN : a.in_dtype;  // IN: the type known at compile time
   if (in_dt == kF16 && pair_aligned(q, kF16)) {
-    gather_q_pairs<N, NCT, HD>(a.group, row0, tid, x, [q](size_t i) {
+    gather_q_pairs<N, NCT, HD>(gsize, row0, tid, x, [q](size_t i) {
       return __half22float2(*reinterpret_cast<const __half2*>(static_cast<const __half*>(q) + i));
     });
   } else if (in_dt == kBF16 && pair_aligned(q, kBF16)) {
-    gather_q_pairs<N, NCT, HD>(a.group, row0, tid, x, [q](size_t i) {
+    gather_q_pairs<N, NCT, HD>(gsize, row0, tid, x, [q](size_t i) {
       return __bfloat1622float2(
           *reinterpret_cast<const __nv_bfloat162*>(static_cast<const __nv_bfloat16*>(q) + i));
     });
   } else if (in_dt == kF32 && pair_aligned(q, kF32)) {
-    gather_q_pairs<N, NCT, HD>(a.group, row0, tid, x, [q](size_t i) {
+    gather_q_pairs<N, NCT, HD>(gsize, row0, tid, x, [q](size_t i) {
       return *reinterpret_cast<const float2*>(static_cast<const float*>(q) + i);
     });
   } else {
     const int dt = in_dt;
-    gather_q_pairs<N, NCT, HD>(a.group, row0, tid, x, [q, dt](size_t i) {
+    gather_q_pairs<N, NCT, HD>(gsize, row0, tid, x, [q, dt](size_t i) {
       return make_float2(load_elem(q, i, dt), load_elem(q, i + 1, dt));
     });
   }
@@ -454,16 +455,17 @@ __device__ __forceinline__ void peer_arrive(const PeerOut& po, uint32_t e, uint3
 // The 128 consumer threads write the group's output rows res[hg][0..HD): to
 // the call's output, or, for a head-sharded call, into every rank's output
 // (after every rank has entered the call), then count the CTA.
-template <int HD, int NCT, bool PEER, int OUT = -1>
+template <int HD, int NCT, bool PEER, int OUT = -1, int GRP = 0>
 __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, int job, int kvh,
                                           int tid, int* flag) {
   const PeerOut& po = a.peer;
   const bool vec = a.out_vec != 0;
   const int out_dt = OUT >= 0 ? OUT : a.out_dtype;  // OUT: the type known at compile time
+  const int gsize = GRP ? GRP : a.group;
   if (!PEER || po.nranks == 0) {
-    for (int c = tid; c < a.group * (HD / 8); c += NCT) {
+    for (int c = tid; c < gsize * (HD / 8); c += NCT) {
       const int hg = c / (HD / 8), d0 = (c % (HD / 8)) * 8;
-      store8(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d0,
+      store8(a.out, (static_cast<size_t>(job) * a.hq + kvh * gsize + hg) * HD + d0,
              out_dt, res + hg * HD + d0, vec);
     }
     return;
@@ -472,10 +474,10 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
   if (tid == 0) flag[1] = peer_wait_entered(po, e, a.status);
   bar_consumers<NCT>();
   if (flag[1]) {
-    for (int c = tid; c < a.group * (HD / 8); c += NCT) {
+    for (int c = tid; c < gsize * (HD / 8); c += NCT) {
       const int hg = c / (HD / 8), d0 = (c % (HD / 8)) * 8;
       const size_t off =
-          (static_cast<size_t>(job) * po.hq_total + po.head_base + kvh * a.group + hg) * HD + d0;
+          (static_cast<size_t>(job) * po.hq_total + po.head_base + kvh * gsize + hg) * HD + d0;
       for (int p = 0; p < po.nranks; ++p)
         store8(po.out[p], off, out_dt, res + hg * HD + d0, vec);
     }
@@ -490,14 +492,16 @@ __device__ __forceinline__ void emit_rows(const AttnArgs& a, const float* res, i
 
 // CL: the launch is clustered (a.cluster > 1); PEER: a head-sharded call
 // (a.peer.nranks > 0); IO: the input and output type when both are known
-// (-1: read from the arguments).  Compile-time facts, so that each form holds
+// (-1: read from the arguments); GRP: the query heads per KV head when known
+// (0: read from the arguments).  Compile-time facts, so that each form holds
 // only its own merge, exchange and conversions: the code a launch runs is
 // fetched cold, and less of it is faster.
-template <int HD, int DT, bool DEVROPE, int KG, bool CL, bool PEER, int IO>
+template <int HD, int DT, bool DEVROPE, int KG, bool CL, bool PEER, int IO, int GRP>
 __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, DT, KG>::kMinCtas)
     splitkv_kernel(const __grid_constant__ AttnArgs a, const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, int job0) {
   using C = SplitCfg<HD, DT, KG>;
+  const int gsize = GRP ? GRP : a.group;  // GRP: the group size known at compile time
   constexpr int NCW = C::kConsumerWarps;  // consumer warps; warp NCW is the producer
   constexpr int NCT = C::kConsumers;
   constexpr bool Q8 = C::kQ8;
@@ -611,8 +615,8 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     int bytes = 0;
     if (warp == 0) {
       base = static_cast<const char*>(a.q) +
-             (static_cast<size_t>(job) * a.hq + kvh * a.group) * HD * ib;
-      bytes = a.group * HD * ib;
+             (static_cast<size_t>(job) * a.hq + kvh * gsize) * HD * ib;
+      bytes = gsize * HD * ib;
     } else if (warp == 1 && !DEVROPE) {
       base = reinterpret_cast<const char*>(a.rope + static_cast<size_t>(qpos) * a.rope_stride);
       bytes = HD / 2 * 16;
@@ -724,7 +728,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   // g the high part of head g, row g+8 the remainder.  Q8_0: int8 fragments
   // (q8_frag_byte) and the per-head factor that turns the integer dot
   // products back into scores.
-  const size_t qrow0 = (static_cast<size_t>(job) * a.hq + kvh * a.group) * HD;
+  const size_t qrow0 = (static_cast<size_t>(job) * a.hq + kvh * gsize) * HD;
   uint32_t* qfrag = reinterpret_cast<uint32_t*>(qs);                  // Q8_0: [HD/32][32][4]
   float* qfac = reinterpret_cast<float*>(qfrag + (HD / 32) * 32 * 4);  // Q8_0: [8]
   if constexpr (Q8) {
@@ -733,12 +737,12 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     float* qmax = qfac + 8;                   // [8 heads][HD / 64 warps]
     float y[kIt][2];
     float2 xq[kIt];
-    load_q_pairs<kIt, NCT, HD, IO>(a, qrow0, threadIdx.x, xq);
+    load_q_pairs<kIt, NCT, HD, IO, GRP>(a, qrow0, threadIdx.x, xq);
 #pragma unroll
     for (int it = 0; it < kIt; ++it) {
       const int idx = threadIdx.x + it * NCT, hg = idx / (HD / 2), p = idx % (HD / 2);
       y[it][0] = y[it][1] = 0.f;
-      if (hg < a.group) rope_pair(xq[it].x, xq[it].y, rope_cs<DEVROPE>(rsrc, p, HD), y[it][0], y[it][1]);
+      if (hg < gsize) rope_pair(xq[it].x, xq[it].y, rope_cs<DEVROPE>(rsrc, p, HD), y[it][0], y[it][1]);
       float mx = fmaxf(fabsf(y[it][0]), fabsf(y[it][1]));
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -769,13 +773,13 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   } else {
     constexpr int kQIt = (8 * (HD / 2) + NCT - 1) / NCT;
     float2 xq[kQIt];
-    load_q_pairs<kQIt, NCT, HD, IO>(a, qrow0, threadIdx.x, xq);
+    load_q_pairs<kQIt, NCT, HD, IO, GRP>(a, qrow0, threadIdx.x, xq);
 #pragma unroll
     for (int it = 0; it < kQIt; ++it) {
       const int idx = threadIdx.x + it * NCT, hg = idx / (HD / 2), p = idx % (HD / 2);
       if (idx >= 8 * (HD / 2)) break;
       float y0 = 0.f, y1 = 0.f;
-      if (hg < a.group) rope_pair(xq[it].x, xq[it].y, rope_cs<DEVROPE>(rsrc, p, HD), y0, y1);
+      if (hg < gsize) rope_pair(xq[it].x, xq[it].y, rope_cs<DEVROPE>(rsrc, p, HD), y0, y1);
       float h0, l0, h1, l1;
       split16<BF>(y0, h0, l0);
       split16<BF>(y1, h1, l1);
@@ -1043,7 +1047,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   }
   // Each thread forms its head's weights itself (a few exponentials, no
   // serial step and no barrier) and sums four columns over the warps.
-  for (int c = tid; c < a.group * (HD / 4); c += NCT) {
+  for (int c = tid; c < gsize * (HD / 4); c += NCT) {
     const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
     float M = -CUDART_INF_F;
 #pragma unroll
@@ -1092,7 +1096,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     // (max, sum) of the group's heads); once they have landed (bounded wait,
     // acquire at cluster scope) it merges the live splits by LSE weight, each
     // thread forming its head's weights, and stores its four columns.
-    const uint32_t push_bytes = a.group * (HD * 4 + 8);
+    const uint32_t push_bytes = gsize * (HD * 4 + 8);
     bar_consumers<NCT>();  // its own res and cml are complete
     if (tid == 0) mbar_arrive_expect_tx(gbar, (nsplit - 1) * push_bytes);
     mbar_wait_cluster(gbar, 0, a.status);
@@ -1111,7 +1115,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     float* mh = mw + 16 * 8;   // [2][4 warps][8 heads]: maxima, then denominators
     if constexpr (KG == 1) {
       const int r = tid >> 3, hg = tid & 7, cw = tid >> 5;
-      const bool live = r < nsplit && hg < a.group;
+      const bool live = r < nsplit && hg < gsize;
       const float m_r = live ? (r == 0 ? cml[2 * hg] : gml[r * 16 + 2 * hg]) : -CUDART_INF_F;
       const float l_r = live ? (r == 0 ? cml[2 * hg + 1] : gml[r * 16 + 2 * hg + 1]) : 0.f;
       float M = fmaxf(m_r, __shfl_xor_sync(0xffffffffu, m_r, 8));
@@ -1128,7 +1132,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
     }
     auto merge = [&](auto width) {
       constexpr int N = decltype(width)::value;
-      for (int c = tid; c < a.group * (HD / 4); c += NCT) {
+      for (int c = tid; c < gsize * (HD / 4); c += NCT) {
         const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
         const float den = (mh[32 + hg] + mh[40 + hg]) + (mh[48 + hg] + mh[56 + hg]);
         // two accumulators halve the dependent chain of multiply-adds
@@ -1149,7 +1153,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
         const float4 out = make_float4((acc[0].x + acc[1].x) * inv, (acc[0].y + acc[1].y) * inv,
                                        (acc[0].z + acc[1].z) * inv, (acc[0].w + acc[1].w) * inv);
         if (direct)
-          store4(a.out, (static_cast<size_t>(job) * a.hq + kvh * a.group + hg) * HD + d0,
+          store4(a.out, (static_cast<size_t>(job) * a.hq + kvh * gsize + hg) * HD + d0,
                  IO >= 0 ? IO : a.out_dtype, out, a.out_vec != 0);
         else
           *reinterpret_cast<float4*>(res + hg * HD + d0) = out;
@@ -1161,13 +1165,13 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
       merge(std::integral_constant<int, 8>{});
     if (!direct) {
       bar_consumers<NCT>();
-      emit_rows<HD, NCT, PEER, IO>(a, res, job, kvh, tid, flag);
+      emit_rows<HD, NCT, PEER, IO, GRP>(a, res, job, kvh, tid, flag);
     }
     return;
   }
   if (nsplit == 1) {
     bar_consumers<NCT>();
-    emit_rows<HD, NCT, PEER, IO>(a, res, job, kvh, tid, flag);
+    emit_rows<HD, NCT, PEER, IO, GRP>(a, res, job, kvh, tid, flag);
     return;
   }
   // ---- the last CTA of this (job, kv head) merges the splits
@@ -1188,7 +1192,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   // Each thread sums four output columns over the splits with a running
   // maximum, loading kU splits' (max, sum) and rows at a time: one round
   // trip to L2 per kU splits.
-  for (int c = tid; c < a.group * (HD / 4); c += NCT) {
+  for (int c = tid; c < gsize * (HD / 4); c += NCT) {
     const int hg = c / (HD / 4), d0 = (c % (HD / 4)) * 4;
     const float4* po = reinterpret_cast<const float4*>(a.part_o + (pslot * 8 + hg) * HD + d0);
     const float2* pm = reinterpret_cast<const float2*>(a.part_ml + (pslot * 8 + hg) * 2);
@@ -1233,7 +1237,7 @@ __global__ void __launch_bounds__(SplitCfg<HD, DT, KG>::kThreads, SplitCfg<HD, D
   }
   if (tid == 0) a.counters[static_cast<size_t>(job) * hkv + kvh] = 0;
   bar_consumers<NCT>();
-  emit_rows<HD, NCT, PEER, IO>(a, res, job, kvh, tid, flag);
+  emit_rows<HD, NCT, PEER, IO, GRP>(a, res, job, kvh, tid, flag);
 }
 
 // ------------------------------------------------ head-sharded exchange --
@@ -1329,20 +1333,25 @@ bool splitkv_supported(int hd, int dtype, int group, int page) {
 using SplitKvFn = void (*)(const AttnArgs, const CUtensorMap, const CUtensorMap, int);
 
 // The compiled form for a launch: clustered or not, head-sharded or not, and
-// (single-GPU calls with the table's RoPE) I/O of the cache's own 16-bit type.
+// (single-GPU calls with the table's RoPE) I/O of the cache's own 16-bit type,
+// then also eight query heads per KV head when the call has that.
 template <int HD, int DT, bool DEVROPE, int KG>
-static SplitKvFn splitkv_form(bool clustered, bool peer, bool io) {
+static SplitKvFn splitkv_form(bool clustered, bool peer, bool io, bool g8) {
   constexpr int kIO = DT == kQ8_0 ? -1 : DT;
   if constexpr (KG == 1) {
     if (clustered) {
-      if (peer) return splitkv_kernel<HD, DT, DEVROPE, KG, true, true, -1>;
-      if (io && !DEVROPE) return splitkv_kernel<HD, DT, DEVROPE, KG, true, false, kIO>;
-      return splitkv_kernel<HD, DT, DEVROPE, KG, true, false, -1>;
+      if (peer) return splitkv_kernel<HD, DT, DEVROPE, KG, true, true, -1, 0>;
+      if (io && !DEVROPE)
+        return g8 ? splitkv_kernel<HD, DT, DEVROPE, KG, true, false, kIO, 8>
+                  : splitkv_kernel<HD, DT, DEVROPE, KG, true, false, kIO, 0>;
+      return splitkv_kernel<HD, DT, DEVROPE, KG, true, false, -1, 0>;
     }
   }
-  if (peer) return splitkv_kernel<HD, DT, DEVROPE, KG, false, true, -1>;
-  if (io && !DEVROPE) return splitkv_kernel<HD, DT, DEVROPE, KG, false, false, kIO>;
-  return splitkv_kernel<HD, DT, DEVROPE, KG, false, false, -1>;
+  if (peer) return splitkv_kernel<HD, DT, DEVROPE, KG, false, true, -1, 0>;
+  if (io && !DEVROPE)
+    return g8 ? splitkv_kernel<HD, DT, DEVROPE, KG, false, false, kIO, 8>
+              : splitkv_kernel<HD, DT, DEVROPE, KG, false, false, kIO, 0>;
+  return splitkv_kernel<HD, DT, DEVROPE, KG, false, false, -1, 0>;
 }
 
 template <int HD, int DT, bool DEVROPE, int KG>
@@ -1359,10 +1368,10 @@ static cudaError_t configure_splitkv_t(int* ctas_per_sm) {
   }
   // every compiled form: shared memory (clustered forms add the gather area)
   // and, for clusters above 8 CTAs, the non-portable size
-  for (int form = 0; form < 8 && e == cudaSuccess; ++form) {
-    const bool clustered = form & 1, peer = form & 2, io = form & 4;
+  for (int form = 0; form < 16 && e == cudaSuccess; ++form) {
+    const bool clustered = form & 1, peer = form & 2, io = form & 4, g8 = form & 8;
     if (clustered && KG != 1) continue;
-    SplitKvFn k = splitkv_form<HD, DT, DEVROPE, KG>(clustered, peer, io);
+    SplitKvFn k = splitkv_form<HD, DT, DEVROPE, KG>(clustered, peer, io, g8);
     e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(clustered ? C::kSmemCluster : C::kSmem));
     if (e == cudaSuccess && clustered && C::kMaxCluster > 8)
@@ -1371,7 +1380,7 @@ static cudaError_t configure_splitkv_t(int* ctas_per_sm) {
   if (e != cudaSuccess) return e;
   int n = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
-      &n, splitkv_form<HD, DT, DEVROPE, KG>(false, false, false), C::kThreads, C::kSmem);
+      &n, splitkv_form<HD, DT, DEVROPE, KG>(false, false, false, false), C::kThreads, C::kSmem);
   if (e != cudaSuccess) return e;
   n = max(n, 1);
   if (dev < kMaxDev) occupancy[dev].store(n, std::memory_order_release);
@@ -1386,8 +1395,8 @@ static cudaError_t launch_splitkv_t(const AttnArgs& a, const CUtensorMap* kmap,
   cudaError_t e = configure_splitkv_t<HD, DT, DEVROPE, KG>(nullptr);
   if (e != cudaSuccess) return e;
   const bool io = DT != kQ8_0 && a.in_dtype == DT && a.out_dtype == DT;
-  const SplitKvFn kernel =
-      splitkv_form<HD, DT, DEVROPE, KG>(KG == 1 && a.cluster > 1, a.peer.nranks > 0, io);
+  const SplitKvFn kernel = splitkv_form<HD, DT, DEVROPE, KG>(KG == 1 && a.cluster > 1,
+                                                             a.peer.nranks > 0, io, a.group == 8);
   for (int j0 = 0; j0 < jobs; j0 += 65535) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.max_splits, a.cache.hkv, min(65535, jobs - j0));
