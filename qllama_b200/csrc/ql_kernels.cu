@@ -1328,8 +1328,6 @@ bool splitkv_supported(int hd, int dtype, int group, int page) {
   return (dtype == kF16 || dtype == kBF16) && (hd == 64 || hd == 128);
 }
 
-// Sets the kernel's shared-memory limit on the current device (once per
-// device) and reports how many of its CTAs an SM holds.
 using SplitKvFn = void (*)(const AttnArgs, const CUtensorMap, const CUtensorMap, int);
 
 // The compiled form for a launch: clustered or not, head-sharded or not, and
@@ -1354,6 +1352,8 @@ static SplitKvFn splitkv_form(bool clustered, bool peer, bool io, bool g8) {
   return splitkv_kernel<HD, DT, DEVROPE, KG, false, false, -1, 0>;
 }
 
+// Sets every form's shared-memory limit on the current device (once per
+// device) and reports how many of the kernel's CTAs an SM holds.
 template <int HD, int DT, bool DEVROPE, int KG>
 static cudaError_t configure_splitkv_t(int* ctas_per_sm) {
   using C = SplitCfg<HD, DT, KG>;
